@@ -1,0 +1,353 @@
+#!/usr/bin/env python
+"""bench.py — decode attention KV GB/s on BASELINE config 2.
+
+Workload (per rank, weak scaling): Llama-3-8B-shaped batched GQA decode,
+B = 32 sequences, 32 query / 8 KV heads, head_dim 128, fp16 KV cache, one new
+token per sequence, KV lengths ~ U[512, 8192] from a per-rank seed, Q/K/V
+~ N(0, 1). The KV bytes (~570 MB per rank) exceed the 126 MB L2, so no flush
+is needed between steps.
+
+  value    device-resident: the decode attention call (split-KV kernel +
+           combine) on inputs already in HBM, CUDA events on its stream.
+  e2e      the same metric through the host-buffer C-ABI call
+           aspida_attn_step_host: H2D of q/k/v/pos from pinned memory, RoPE
+           + K/V append, decode, D2H of the output, every step.
+  roofline algorithmic bytes per call / average call time vs the measured HBM
+           copy bandwidth (MEASURED_PEAKS.json).
+  cpu_baseline  the CPU oracle (C++ restatement of the reference's Ada loops)
+           on the box's host cores, rank 0 at N=1.
+
+--impl reference times that CPU implementation as the reference arm.
+Launch: python bench.py [--gpus N --steps K --warmup W]; for N > 1 under
+torch.distributed.run (one rank per GPU, NCCL).
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+NQ, NKV, HD, B = 32, 8, 128, 32
+LEN_LO, LEN_HI = 512, 8192
+METRIC = "decode attn KV GB/s (cfg2: Llama-3-8B GQA decode B32, 32/8 heads, hd128, fp16 KV)"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def seq_lens(seed):
+    return np.random.RandomState(seed).randint(LEN_LO, LEN_HI + 1, size=B).tolist()
+
+
+def algo_bytes(lens):
+    kv = sum(lens) * NKV * HD * 2 * 2          # K and V, fp16
+    qo = B * NQ * HD * (4 + 4)                 # f32 query in, f32 output out
+    return kv + qo
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profile():
+    """dram bytes per decode call from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "decode_cfg2.md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.startswith("traffic_bytes_per_call:"):
+            try:
+                return int(line.split(":", 1)[1].strip())
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+def cpu_baseline(lens_list, seconds, K_host, V_host, q_host):
+    """Time the oracle on the host cores over the full cfg-2 batch."""
+    import oracle
+    threads = os.cpu_count() or 1
+    oracle.load()
+    reps, t0 = 0, time.perf_counter()
+    pos = [L - 1 for L in lens_list]
+    while True:
+        oracle.decode_batch(q_host, K_host, V_host, pos, NQ, NKV, HD, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 1000:
+            break
+    per = el / reps
+    return {"value": algo_bytes(lens_list) / per / 1e9, "unit": "GB/s", "cores": threads,
+            "kind": "port",
+            "sample": f"full cfg-2 batch (B=32, {sum(lens_list)} keys), {reps} reps in {el:.1f} s, "
+                      "C++ restatement of the Ada attention loops, one (seq x head) job per task"}
+
+
+def host_batch(seed, lens):
+    """Same values as the device batch, as fp32 host arrays for the oracle."""
+    import torch
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    Ks, Vs = [], []
+    for L in lens:
+        Ks.append(torch.randn(L, NKV * HD, generator=g).half())
+        Vs.append(torch.randn(L, NKV * HD, generator=g).half())
+    q = torch.randn(B, NQ * HD, generator=g)
+    return q, Ks, Vs
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    lens = seq_lens(1000)
+    q, Ks, Vs = host_batch(1000, lens)
+    Kh = [k.float().numpy() for k in Ks]
+    Vh = [v.float().numpy() for v in Vs]
+    qh = q.numpy()
+    import oracle
+    oracle.load()
+    threads = os.cpu_count() or 1
+    pos = [L - 1 for L in lens]
+    for _ in range(max(1, min(args.warmup, 2))):
+        oracle.decode_batch(qh, Kh, Vh, pos, NQ, NKV, HD, threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        oracle.decode_batch(qh, Kh, Vh, pos, NQ, NKV, HD, threads=threads)
+        times.append(time.perf_counter() - t0)
+        if sum(times) > 120:
+            break
+    per = sum(times) / len(times)
+    val = algo_bytes(lens) / per / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "cfg2 batched GQA decode (B=32, 32/8, hd128, len~U[512,8192])",
+                   "global_batch": B, "parallelism": "rank 0 only (host CPU)"},
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"full cfg-2 batch, {len(times)} timed steps"},
+        "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+
+    import torch
+    import aspida_b200 as ab
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+
+    seed = 1000 + rank
+    lens = seq_lens(seed)
+    q_h, Ks_h, Vs_h = host_batch(seed, lens)
+    caches = [ab.KVCache(L, NKV, HD, NQ) for L in lens]
+    for c, k, v in zip(caches, Ks_h, Vs_h):
+        c.K.copy_(k)
+        c.V.copy_(v)
+    q = q_h.to(dev)
+    Kt = ab.ptr_table([c.K for c in caches], dev)
+    Vt = ab.ptr_table([c.V for c in caches], dev)
+    pos = torch.tensor([L - 1 for L in lens], dtype=torch.int32, device=dev)
+    out = torch.empty(B, NQ * HD, device=dev)
+    ws = ab.Workspace()
+    stream = torch.cuda.current_stream()
+    maxkv = max(lens)
+
+    def step():
+        ab.decode(q, Kt, Vt, pos, NQ, NKV, HD, max_kv_len=maxkv, out=out, workspace=ws,
+                  stream=stream)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    t_end = time.perf_counter() + 1.5        # keep the GPU under load for clock samples
+    while time.perf_counter() < t_end:
+        for _ in range(50):
+            step()
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / args.steps
+    if dist:
+        dist.barrier()
+    status = ab.device_status()
+    if status != 0:
+        raise RuntimeError(f"device status {status}")
+
+    # ---- e2e through the host-buffer C-ABI call ----
+    qp = q_h.clone().pin_memory()
+    kp = torch.randn(B, NKV * HD).pin_memory()
+    vp = torch.randn(B, NKV * HD).pin_memory()
+    op = torch.empty(B, NQ * HD).pin_memory()
+    handles = [c.handle for c in caches]
+    pos_l = [L - 1 for L in lens]
+    for _ in range(max(3, args.warmup)):
+        ab.step_host(handles, qp, kp, vp, pos_l, op, NQ, NKV, HD, rope_dim=HD,
+                     rope_base=500000.0, stream=stream)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        ab.step_host(handles, qp, kp, vp, pos_l, op, NQ, NKV, HD, rope_dim=HD,
+                     rope_base=500000.0, stream=stream)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    ms_e2e = f0.elapsed_time(f1) / args.steps
+
+    nbytes = algo_bytes(lens)
+    stats = torch.tensor([ms, ms_e2e, float(nbytes)], dtype=torch.float64, device=dev)
+    if dist:
+        mx = stats[:2].clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = stats[2:].clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_max, ms_e2e_max, bytes_all = float(mx[0]), float(mx[1]), float(tot[0])
+    else:
+        ms_max, ms_e2e_max, bytes_all = ms, ms_e2e, float(nbytes)
+
+    if rank == 0:
+        hbm, src = peaks()
+        achieved = nbytes / (ms * 1e-3) / 1e9
+        traffic = traffic_from_profile()
+        line = {
+            "metric": METRIC,
+            "value": round(bytes_all / (ms_max * 1e-3) / 1e9, 3),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_max, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "f16 KV / f32 accumulate",
+            "data": "synthetic (seeded N(0,1) fp16 KV, lengths U[512,8192])",
+            "config": {"workload": "cfg2 batched GQA decode: B=32 per GPU, 32/8 heads, hd128, "
+                                   "fp16 KV, len~U[512,8192]",
+                       "global_batch": B * world, "kv_bytes_per_gpu": nbytes,
+                       "parallelism": f"dp{world} (sequence sharding, no collective)",
+                       "l2": "inputs (~570 MB KV per GPU) larger than the 126 MB L2; no flush"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
+                         "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": traffic, "peak_source": f"{src} hbm_gbs (copy, burst)"},
+            "e2e": {"value": round(bytes_all / (ms_e2e_max * 1e-3) / 1e9, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(qp.numel() * 4 + kp.numel() * 4 + vp.numel() * 4
+                                              + B * (2 * 4 + 2 * 8)),
+                    "d2h_bytes_per_step": int(op.numel() * 4),
+                    "ms_per_step": round(ms_e2e_max, 5)},
+            "gpu_launches": args.steps * 2,
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(lens, args.cpu_seconds,
+                                                [k.float().numpy() for k in Ks_h],
+                                                [v.float().numpy() for v in Vs_h], q_h.numpy())
+        print(json.dumps(line), flush=True)
+    for c in caches:
+        c.free()
+    if dist:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

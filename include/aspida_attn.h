@@ -1,0 +1,172 @@
+/*
+ * aspida_attn.h — C ABI of libaspida_attn.so, the B200 (sm_100a) attention
+ * library for the Aspida inference engine.
+ *
+ * The library is a drop-in for the attention part of Aspida's dlopen'd GPU
+ * shim (libaspidagpu.so). Citations name the reference interface each entry
+ * replaces, as path:line inside the reference project.
+ *
+ * Conventions
+ *  - Every pointer marked "dev" is CUDA device memory; "host" is host memory.
+ *  - KV layout is the shim's: fp16, row-major [max_len][nkv*hd], i.e.
+ *    [pos][kv_head][dim], one row per position (gpu/gpu_matvec.cu:1312).
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).
+ *  - Entry points returning int return 0 on success, a negative ASPIDA_ERR_*
+ *    for argument/state errors, or a positive cudaError_t value. Every
+ *    non-zero status is also latched for aspida_gpu_last_error().
+ *  - No CPU fallback: a shape the kernels do not support is rejected with
+ *    ASPIDA_ERR_UNSUPPORTED.
+ *  - Calls on distinct streams may run concurrently; scratch memory is either
+ *    caller-provided (workspace) or owned by the KV state / per stream.
+ */
+#ifndef ASPIDA_ATTN_H
+#define ASPIDA_ATTN_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ASPIDA_OK 0
+#define ASPIDA_ERR_ARG (-1)         /* bad argument (sizes, null pointers)   */
+#define ASPIDA_ERR_HANDLE (-2)      /* unknown or freed handle / slot        */
+#define ASPIDA_ERR_NOMEM (-3)       /* device allocation failed              */
+#define ASPIDA_ERR_UNSUPPORTED (-4) /* shape outside the kernels' coverage   */
+#define ASPIDA_ERR_WORKSPACE (-5)   /* caller workspace smaller than needed  */
+#define ASPIDA_ERR_DEVICE (-6)      /* a kernel's bounded wait ran out       */
+
+/* ------------------------------------------------------------------------
+ * KV-state lifecycle
+ * ------------------------------------------------------------------------ */
+
+/* Allocate a resident fp16 K/V cache of max_len rows x kvd halves each.
+ * Returns a handle >= 0, or -1 on failure (bad sizes / allocation failure).
+ * `nq` is accepted for signature compatibility; this library keeps no
+ * per-head score scratch, so it only participates in argument checking.
+ * Replaces aspida_gpu_fattn_new, gpu/gpu_matvec.cu:1316. */
+int aspida_gpu_fattn_new(int max_len, int kvd, int nq);
+
+/* Synchronise the device, then release the state; the handle is reused.
+ * Unknown handles are ignored. Replaces gpu/gpu_matvec.cu:1335. */
+void aspida_gpu_fattn_free(int handle);
+
+/* Copy the first `rows` K/V rows of `handle` into a retained snapshot slot
+ * (slot = -1 allocates a new one; an existing slot of the same rows/kvd is
+ * overwritten in place). Returns the slot, or -1.
+ * Replaces aspida_gpu_fattn_snapshot, gpu/gpu_matvec.cu:1359. */
+int aspida_gpu_fattn_snapshot(int handle, int rows, int slot);
+
+/* Copy snapshot `slot` back into rows 0..rows-1 of `handle`. Returns 0 or -1.
+ * Replaces aspida_gpu_fattn_restore, gpu/gpu_matvec.cu:1391. */
+int aspida_gpu_fattn_restore(int handle, int slot);
+
+/* Free every retained snapshot. Replaces gpu/gpu_matvec.cu:1409. */
+void aspida_gpu_prefix_reset(void);
+
+/* Return and clear the first non-zero status latched since the last call
+ * (or a pending CUDA error). 0 = no error.
+ * Replaces aspida_gpu_last_error, gpu/gpu_matvec.cu:2348. */
+int aspida_gpu_last_error(void);
+
+/* Device pointers and geometry of a state (no counterpart in the shim, where
+ * the state is only reachable inside the library; exported so a caller can
+ * run the attention entry points below on handle-owned caches).
+ * Returns 0 or ASPIDA_ERR_HANDLE. Any output pointer may be NULL. */
+int aspida_gpu_fattn_kv(int handle, void** K, void** V, int* max_len, int* kvd);
+
+/* Synchronise the current device and return (then clear) the device status
+ * word that a kernel sets when one of its bounded waits runs out:
+ * 0 = none, ASPIDA_ERR_DEVICE otherwise. */
+int aspida_attn_device_status(void);
+
+/* Test hook: make the next `n` device allocations made by the library fail
+ * (as cudaMalloc would on an exhausted device). n = 0 disarms it. */
+void aspida_attn_debug_fail_allocs(int n);
+
+/* ------------------------------------------------------------------------
+ * Pre-attention step: per-head RMSNorm (optional), partial RoPE, and the
+ * fp16 K/V append for P consecutive tokens at positions pos_start..+P-1.
+ * Replaces k_fattn_prep / k_fattn_prep_chunk (gpu/gpu_matvec.cu:1449-1503,
+ * 3235-3292) and the RoPE of LLM_RoPE.Apply_Sections (src/llm/llm_rope.adb:84).
+ *   q      dev f32 [P][nq*hd]    raw query rows (gate already split off)
+ *   k, v   dev f32 [P][nkv*hd]   raw key / value rows
+ *   q_norm, k_norm  dev f32 [hd] RMSNorm weights, or NULL for no QK-norm
+ *   q_out  dev [P][nq*hd], f32 (q_out_fp16 = 0) or fp16 (q_out_fp16 = 1)
+ *   K, V   dev fp16 cache [max_len][nkv*hd]; rows pos_start..+P-1 written
+ *   RoPE:  rd rotated dims (<= hd, even), base, freq_scale (PI), m_scale,
+ *          yarn_on/corr_lo/corr_hi (YaRN ramp), ff dev [rd/2] (use_ff),
+ *          interleaved (adjacent pairs) or NeoX split-half, sec_total:
+ *          pairs i >= sec_total use position 0 (reference section quirk;
+ *          pass rd/2 to rotate every pair).
+ * ------------------------------------------------------------------------ */
+int aspida_attn_prep(const float* q, const float* k, const float* v, int P, int nq, int nkv,
+                     int hd, const float* q_norm, const float* k_norm, float eps, void* q_out,
+                     int q_out_fp16, void* K, void* V, int max_len, int pos_start, int rd,
+                     float base, float freq_scale, float m_scale, int yarn_on, float corr_lo,
+                     float corr_hi, const float* ff, int use_ff, int interleaved, int sec_total,
+                     void* stream);
+
+/* ------------------------------------------------------------------------
+ * Decode attention (one new token per sequence, GQA, split-KV).
+ * Replaces the k_fattn_attend / k_fattn_attend_b launches
+ * (gpu/gpu_matvec.cu:1507-1609, called at 2303-2304 and 2887-2892).
+ *   q        dev f32 [B][nq*hd]  roped queries
+ *   gate     dev f32 [B][nq*hd]  or NULL; out *= sigmoid(gate) (Qwen gate)
+ *   K, V     dev tables [B] of dev fp16 caches [rows][nkv*hd]
+ *   pos      dev i32 [B]  0-based position of the new token: keys 0..pos
+ *   max_len  dev i32 [B]  or NULL: keys are clamped below max_len[b]
+ *   out      dev f32 [B][nq*hd]
+ *   scale    softmax scale (1/sqrt(hd) for Llama/Qwen, 1.0 for Gemma)
+ *   window   sliding window (keys max(0,pos-window+1)..pos), 0 = none
+ *   softcap  s <- softcap*tanh(s/softcap) after scaling, 0 = none
+ *   max_kv_len  upper bound of pos+1 over the batch (sizes the split)
+ *   chunk    keys per split (multiple of 64), 0 = automatic
+ *   workspace/workspace_bytes  dev scratch >= aspida_attn_decode_workspace_size
+ * Supported: hd in {64,128,256}, nq % nkv == 0, nq/nkv <= 8.
+ * ------------------------------------------------------------------------ */
+size_t aspida_attn_decode_workspace_size(int B, int nq, int nkv, int hd, int max_kv_len,
+                                         int chunk);
+int aspida_attn_decode(const float* q, const float* gate, const void* const* K,
+                       const void* const* V, const int* pos, const int* max_len, float* out,
+                       int B, int nq, int nkv, int hd, float scale, int window, float softcap,
+                       int max_kv_len, int chunk, void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Split-KV partial for sequence-parallel decode: attend keys
+ * kv_lo[b]..kv_hi[b]-1 of each cache and write the unnormalised partial
+ * (m = running max in natural-log units, l = sum of exp(s-m), o = sum of
+ * exp(s-m)*v) per (sequence, head): m, l dev f32 [B][nq]; o dev f32 [B][nq][hd].
+ * An empty range gives m = -3.4e38, l = 0, o = 0. This is the per-slice half
+ * of flash-decoding split-K (k_splitk, gpu/fattn_sk.cu:38-83), extended to a
+ * slice per GPU. */
+int aspida_attn_decode_partial(const float* q, const void* const* K, const void* const* V,
+                               const int* kv_lo, const int* kv_hi, float* m, float* l, float* o,
+                               int B, int nq, int nkv, int hd, float scale, float softcap,
+                               int max_kv_len, int chunk, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* Log-sum-exp merge of S partials (k_combine, gpu/fattn_sk.cu:84-97):
+ *   m, l dev f32 [S][rows]; o dev f32 [S][rows][hd]; gate dev f32 [rows][hd]
+ *   or NULL; out dev f32 [rows][hd] = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s. */
+int aspida_attn_merge(const float* m, const float* l, const float* o, const float* gate,
+                      float* out, int S, int rows, int hd, void* stream);
+
+/* Host-buffer decode step for B resident states — the attention half of
+ * aspida_gpu_fattn_step / chain_forward_batch (gpu/gpu_matvec.cu:1613, 2783)
+ * without the projections: copies q/k/v/pos from host, runs prep (RoPE, no
+ * QK-norm, KV append at pos[b]) and decode, copies the output to host and
+ * synchronises the stream.
+ *   handles host [B]; q host f32 [B][nq*hd]; k, v host f32 [B][nkv*hd];
+ *   pos host [B]; out host f32 [B][nq*hd]. RoPE: NeoX or interleaved over
+ *   rd dims with base (rd = 0 disables RoPE). */
+int aspida_attn_step_host(const int* handles, int B, const float* q, const float* k,
+                          const float* v, const int* pos, float* out, int nq, int nkv, int hd,
+                          float scale, int window, float softcap, int rd, float base,
+                          int interleaved, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASPIDA_ATTN_H */

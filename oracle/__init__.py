@@ -1,0 +1,163 @@
+"""CPU oracle — TEST INFRASTRUCTURE ONLY.
+
+numpy front end of liboracle_attn.so (attn_oracle.cpp), the C++ restatement
+of the reference's Ada attention loops. Only tests/, __graft_entry__.smoke()
+and bench.py's CPU-baseline legs use it, as the checker; the product path in
+aspida_b200/ never imports it.
+
+Parity is pinned against fixtures produced by the reference's own fp32
+kernels (oracle/ref_harness.cu, tests/golden/make_golden.py) and against the
+reference's known-answer tests restated in tests/test_oracle.py.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle_attn.so")
+
+_lib = None
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def load():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        lib = C.CDLL(LIB_PATH)
+        vp, i32, f32 = C.c_void_p, C.c_int, C.c_float
+        lib.oracle_rmsnorm.argtypes = [vp, vp, vp, i32, f32]
+        lib.oracle_rope_apply_sections.argtypes = [vp, vp, i32, f32, vp, vp, i32, vp, i32, f32,
+                                                   i32, f32, f32, f32]
+        lib.oracle_norm_rope.argtypes = [vp, vp, f32, vp, i32, i32, i32, f32, i32, i32, vp, i32,
+                                         f32, i32, f32, f32, f32]
+        lib.oracle_decode_batch.argtypes = [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32,
+                                            f32, i32]
+        lib.oracle_prefill.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, f32, i32, f32,
+                                       vp, i32, i32]
+        lib.oracle_merge.argtypes = [vp, vp, vp, vp, vp, i32, i32, i32]
+        for fn in ("oracle_rmsnorm", "oracle_rope_apply_sections", "oracle_norm_rope",
+                   "oracle_decode_batch", "oracle_prefill", "oracle_merge"):
+            getattr(lib, fn).restype = None
+        _lib = lib
+    return _lib
+
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data
+
+
+def rmsnorm(x, w, eps=1e-6):
+    x, w = _f32(x), _f32(w)
+    out = np.empty_like(x)
+    load().oracle_rmsnorm(_p(x), _p(w), _p(out), x.size, eps)
+    return out
+
+
+def rope_apply_sections(x, base, sections, sec_pos, *, ff=None, interleaved=False,
+                        freq_scale=1.0, yarn_on=False, corr_lo=0.0, corr_hi=0.0, m_scale=1.0):
+    """LLM_RoPE.Apply_Sections on one head vector of length dim."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    sec = np.ascontiguousarray(sections, dtype=np.int32)
+    sp = np.ascontiguousarray(sec_pos, dtype=np.int32)
+    ffa = _f32(ff) if ff is not None else None
+    load().oracle_rope_apply_sections(_p(x), _p(out), x.size, base, _p(sec), _p(sp),
+                                      int(ff is not None), _p(ffa), int(interleaved), freq_scale,
+                                      int(yarn_on), corr_lo, corr_hi, m_scale)
+    return out
+
+
+def rope_apply(x, base, pos, **kw):
+    """LLM_RoPE.Apply: all pairs at `pos` (sections covering dim/2)."""
+    d = np.asarray(x).size
+    return rope_apply_sections(x, base, [d // 2, 0, 0, 0], [pos] * 4, **kw)
+
+
+def norm_rope(x, norm_w, hd, rd, pos, base, *, eps=1e-6, sec_total=None, ff=None,
+              interleaved=False, freq_scale=1.0, yarn_on=False, corr_lo=0.0, corr_hi=0.0,
+              m_scale=1.0):
+    """Norm_Rope of LLM_FullAttn for one head (norm_w None = no RMSNorm)."""
+    x = _f32(x)
+    out = np.empty(hd, np.float32)
+    nw = _f32(norm_w) if norm_w is not None else None
+    ffa = _f32(ff) if ff is not None else None
+    load().oracle_norm_rope(_p(x), _p(nw), eps, _p(out), hd, rd, pos, base,
+                            rd // 2 if sec_total is None else sec_total, int(ff is not None),
+                            _p(ffa), int(interleaved), freq_scale, int(yarn_on), corr_lo,
+                            corr_hi, m_scale)
+    return out
+
+
+def rope_rows(x, nheads, hd, positions, base, *, rd=None, interleaved=False, sec_total=None):
+    """Rotate rows x[t] ([nheads*hd] each) at positions[t] (no norm)."""
+    x = _f32(x)
+    rd = hd if rd is None else rd
+    out = np.empty_like(x)
+    for t, p in enumerate(positions):
+        for h in range(nheads):
+            out[t, h * hd:(h + 1) * hd] = norm_rope(x[t, h * hd:(h + 1) * hd], None, hd, rd, int(p),
+                                                    base, interleaved=interleaved,
+                                                    sec_total=sec_total)
+    return out
+
+
+def decode_batch(q, K_list, V_list, pos, nq, nkv, hd, *, gate=None, scale=None, window=0,
+                 softcap=0.0, threads=0):
+    """q [B, nq*hd]; K_list/V_list: B arrays [rows, nkv*hd] (f32); pos [B]."""
+    q = _f32(q)
+    B = q.shape[0]
+    Ks = [_f32(k) for k in K_list]
+    Vs = [_f32(v) for v in V_list]
+    kp = (C.c_void_p * B)(*[k.ctypes.data for k in Ks])
+    vp_ = (C.c_void_p * B)(*[v.ctypes.data for v in Vs])
+    posa = np.ascontiguousarray(pos, dtype=np.int32)
+    g = _f32(gate) if gate is not None else None
+    out = np.empty((B, nq * hd), np.float32)
+    if scale is None:
+        scale = 1.0 / np.sqrt(np.float32(hd))
+    threads = threads or os.cpu_count() or 1
+    load().oracle_decode_batch(_p(q), _p(g), C.cast(kp, C.c_void_p), C.cast(vp_, C.c_void_p),
+                               _p(posa), _p(out), B, nq, nkv, hd, float(scale), window, softcap,
+                               threads)
+    return out
+
+
+def prefill(q, K, V, pos_start, nq, nkv, hd, *, gate=None, scale=None, window=0, softcap=0.0,
+            rows=None, threads=0):
+    """q [P, nq*hd]; K/V [pos_start+P, nkv*hd]. rows: optional token subset.
+    Returns [P, nq*hd] (rows not in the subset are left as NaN)."""
+    q, K, V = _f32(q), _f32(K), _f32(V)
+    P = q.shape[0]
+    out = np.full((P, nq * hd), np.nan, np.float32)
+    g = _f32(gate) if gate is not None else None
+    if scale is None:
+        scale = 1.0 / np.sqrt(np.float32(hd))
+    ra = np.ascontiguousarray(rows, dtype=np.int32) if rows is not None else None
+    threads = threads or os.cpu_count() or 1
+    load().oracle_prefill(_p(q), _p(g), _p(K), _p(V), _p(out), P, pos_start, nq, nkv, hd,
+                          float(scale), window, softcap, _p(ra), 0 if ra is None else ra.size,
+                          threads)
+    return out
+
+
+def merge(m, l, o, gate=None):
+    """m, l [S, rows]; o [S, rows, hd] -> [rows, hd]."""
+    m, l, o = _f32(m), _f32(l), _f32(o)
+    S, rows, hd = o.shape
+    g = _f32(gate) if gate is not None else None
+    out = np.empty((rows, hd), np.float32)
+    load().oracle_merge(_p(m), _p(l), _p(o), _p(g), _p(out), S, rows, hd)
+    return out

@@ -1,0 +1,39 @@
+"""CPU checks of the C ABI: the library loads, exports every entry point that
+include/aspida_attn.h declares, and the binding covers exactly those."""
+import ctypes
+import os
+import re
+
+from aspida_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "aspida_attn.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(aspida_\w+)\s*\(", src)))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert "aspida_attn_decode" in syms and "aspida_gpu_fattn_new" in syms
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(_lib.LIB_PATH)
+    missing = [s for s in declared_symbols() if not hasattr(lib, s)]
+    assert not missing, missing
+
+
+def test_binding_matches_header():
+    assert sorted(_lib.SIGNATURES) == declared_symbols()
+
+
+def test_workspace_size_is_host_only_and_monotone():
+    lib = _lib.load()
+    a = lib.aspida_attn_decode_workspace_size(32, 32, 8, 128, 8192, 512)
+    b = lib.aspida_attn_decode_workspace_size(32, 32, 8, 128, 16384, 512)
+    c = lib.aspida_attn_decode_workspace_size(64, 32, 8, 128, 8192, 512)
+    assert 0 < a < b and a < c
+    assert lib.aspida_attn_decode_workspace_size(0, 32, 8, 128, 8192, 512) == 0

@@ -1,0 +1,225 @@
+"""GPU parity of the decode path (prep + split-KV decode + combine) against the
+CPU oracle, through the C ABI of libaspida_attn.so."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from tests.util import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ab():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import aspida_b200
+    return aspida_b200
+
+
+def make_batch(lens, nq, nkv, hd, seed, cap_extra=0, scale_q=1.0):
+    """Random fp16 caches (one allocation per sequence) and f32 queries."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    kvd = nkv * hd
+    Ks = [torch.randn(L + cap_extra, kvd, generator=g, device="cuda").half() for L in lens]
+    Vs = [torch.randn(L + cap_extra, kvd, generator=g, device="cuda").half() for L in lens]
+    q = torch.randn(len(lens), nq * hd, generator=g, device="cuda") * scale_q
+    return q, Ks, Vs
+
+
+def run_decode(ab, q, Ks, Vs, pos, nq, nkv, hd, **kw):
+    Kt = ab.ptr_table(Ks, q.device)
+    Vt = ab.ptr_table(Vs, q.device)
+    p = torch.tensor(pos, dtype=torch.int32, device=q.device)
+    ml = kw.pop("max_len", None)
+    mlt = torch.tensor(ml, dtype=torch.int32, device=q.device) if ml is not None else None
+    mkv = kw.pop("max_kv_len", max(pos) + 1)
+    out = ab.decode(q, Kt, Vt, p, nq, nkv, hd, max_len=mlt, max_kv_len=mkv, **kw)
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    return out.cpu().numpy()
+
+
+def oracle_decode(oracle, q, Ks, Vs, pos, nq, nkv, hd, **kw):
+    return oracle.decode_batch(q.cpu().numpy(), [k.float().cpu().numpy() for k in Ks],
+                               [v.float().cpu().numpy() for v in Vs], pos, nq, nkv, hd, **kw)
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(64, 32, 8), (128, 32, 8), (128, 64, 8), (256, 16, 8),
+                                       (128, 8, 8), (64, 8, 1), (128, 12, 4)])
+def test_decode_shapes(ab, oracle, hd, nq, nkv):
+    lens = [1, 15, 16, 17, 100, 333, 1000, 2049]
+    q, Ks, Vs = make_batch(lens, nq, nkv, hd, seed=hd + nq)
+    pos = [L - 1 for L in lens]
+    got = run_decode(ab, q, Ks, Vs, pos, nq, nkv, hd, chunk=256)
+    ref = oracle_decode(oracle, q, Ks, Vs, pos, nq, nkv, hd)
+    assert_parity(got, ref, what=f"hd{hd} {nq}/{nkv}")
+
+
+@pytest.mark.parametrize("chunk", [64, 128, 512, 4096, 0])
+def test_decode_chunking(ab, oracle, chunk):
+    lens = [700, 64, 65, 4000]
+    q, Ks, Vs = make_batch(lens, 32, 8, 128, seed=7)
+    pos = [L - 1 for L in lens]
+    got = run_decode(ab, q, Ks, Vs, pos, 32, 8, 128, chunk=chunk)
+    ref = oracle_decode(oracle, q, Ks, Vs, pos, 32, 8, 128)
+    assert_parity(got, ref, what=f"chunk {chunk}")
+
+
+def test_decode_window_softcap_gate_scale(ab, oracle):
+    """Gemma-style: sliding window, scale 1.0 / 1/16, attention softcap 50;
+    Qwen-style sigmoid gate."""
+    lens = [10, 1024, 1500, 3000]
+    nq, nkv, hd = 16, 8, 256
+    q, Ks, Vs = make_batch(lens, nq, nkv, hd, seed=9, scale_q=0.25)
+    pos = [L - 1 for L in lens]
+    gate = torch.randn(len(lens), nq * hd, device="cuda")
+    for scale, window, cap, g in [(1.0 / 16, 1024, 50.0, None), (1.0, 1024, 50.0, None),
+                                  (1.0 / 16, 0, 0.0, gate), (1.0 / 16, 7, 0.0, gate)]:
+        got = run_decode(ab, q, Ks, Vs, pos, nq, nkv, hd, scale=scale, window=window,
+                         softcap=cap, gate=g, chunk=256)
+        ref = oracle_decode(oracle, q, Ks, Vs, pos, nq, nkv, hd, scale=scale, window=window,
+                            softcap=cap, gate=None if g is None else g.cpu().numpy())
+        assert_parity(got, ref, what=f"scale {scale} window {window} cap {cap}")
+
+
+def test_decode_max_len_clamp_and_positions(ab, oracle):
+    """pos beyond max_len is clamped to max_len-1 (k_fattn_attend_b, gpu_matvec.cu:1576);
+    positions inside a longer cache attend only keys 0..pos."""
+    lens = [300, 300, 300]
+    q, Ks, Vs = make_batch(lens, 32, 8, 128, seed=3)
+    pos = [299, 120, 0]
+    got = run_decode(ab, q, Ks, Vs, [299, 120, 500], 32, 8, 128, max_len=[300, 300, 1],
+                     chunk=64, max_kv_len=501)
+    ref = oracle_decode(oracle, q, Ks, Vs, pos, 32, 8, 128)
+    assert_parity(got, ref, what="clamp")
+
+
+def test_decode_cfg2_full_size(ab, oracle):
+    """BASELINE config 2 at full size: B=32, 32/8, hd128, len ~ U[512, 8192]."""
+    rng = np.random.RandomState(2)
+    lens = rng.randint(512, 8193, size=32).tolist()
+    q, Ks, Vs = make_batch(lens, 32, 8, 128, seed=2)
+    pos = [L - 1 for L in lens]
+    got = run_decode(ab, q, Ks, Vs, pos, 32, 8, 128)
+    ref = oracle_decode(oracle, q, Ks, Vs, pos, 32, 8, 128)
+    assert_parity(got, ref, what="cfg2")
+
+
+def test_decode_is_deterministic(ab):
+    lens = [5000, 3000]
+    q, Ks, Vs = make_batch(lens, 32, 8, 128, seed=4)
+    pos = [L - 1 for L in lens]
+    a = run_decode(ab, q, Ks, Vs, pos, 32, 8, 128)
+    b = run_decode(ab, q, Ks, Vs, pos, 32, 8, 128)
+    assert np.array_equal(a, b)
+
+
+def test_partial_and_merge(ab, oracle):
+    """Sequence-parallel decode: split the keys of one long sequence into S
+    slices, compute partials, merge; equals whole-range decode."""
+    L, nq, nkv, hd = 20000, 64, 8, 128
+    q, Ks, Vs = make_batch([L], nq, nkv, hd, seed=5)
+    K, V = Ks[0], Vs[0]
+    cuts = [0, 5000, 5001, 12000, 12000, L]     # includes an empty slice
+    ms, ls, os_ = [], [], []
+    for a, b in zip(cuts[:-1], cuts[1:]):
+        # each slice is its own "local cache" (as on its GPU): rows a..b-1
+        Kt = ab.ptr_table([K[a:] if a < L else K], q.device)
+        Vt = ab.ptr_table([V[a:] if a < L else V], q.device)
+        lo = torch.tensor([0], dtype=torch.int32, device="cuda")
+        hi = torch.tensor([b - a], dtype=torch.int32, device="cuda")
+        m, l, o = ab.decode_partial(q, Kt, Vt, lo, hi, nq, nkv, hd, max_kv_len=max(1, b - a))
+        ms.append(m); ls.append(l); os_.append(o)
+    m = torch.stack(ms).reshape(len(ms), -1)
+    l = torch.stack(ls).reshape(len(ls), -1)
+    o = torch.stack(os_).reshape(len(os_), nq, hd)
+    out = ab.merge(m, l, o).reshape(1, -1).cpu().numpy()
+    ref = oracle_decode(oracle, q, Ks, Vs, [L - 1], nq, nkv, hd)
+    assert_parity(out, ref, what="partial+merge")
+    # the empty slice reports m = -3.4e38, l = 0
+    assert float(ms[3].max()) < -3e38 and float(ls[3].abs().max()) == 0.0
+
+
+def test_prep_rope_and_append(ab, oracle):
+    """prep == oracle Norm_Rope, with and without QK-norm, NeoX and
+    interleaved, partial rotary (rd < hd), reference section quirk."""
+    P, nq, nkv, hd, ps = 5, 8, 2, 128, 1000
+    g = torch.Generator(device="cuda").manual_seed(1)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda")
+    k = torch.randn(P, nkv * hd, generator=g, device="cuda")
+    v = torch.randn(P, nkv * hd, generator=g, device="cuda")
+    qn = torch.rand(hd, generator=g, device="cuda") + 0.5
+    kn = torch.rand(hd, generator=g, device="cuda") + 0.5
+    cache = ab.KVCache(ps + P + 3, nkv, hd, nq)
+    for rd, inter, norm, sec in [(hd, False, False, None), (hd, True, False, None),
+                                 (64, False, True, None), (hd, False, True, 32)]:
+        rope = ab.RopeParams(dim=rd, freq_base=500000.0, interleaved=inter,
+                             sections=() if sec is None else (sec, 0, 0, 0))
+        qo = ab.prep(q, k, v, cache.K, cache.V, ps, nq, nkv, hd, rope,
+                     q_norm=qn if norm else None, k_norm=kn if norm else None)
+        torch.cuda.synchronize()
+        qn_h, kn_h = (qn.cpu().numpy(), kn.cpu().numpy()) if norm else (None, None)
+        for t in range(P):
+            for h in range(nq):
+                exp = oracle.norm_rope(q[t, h * hd:(h + 1) * hd].cpu().numpy(), qn_h, hd, rd, ps + t,
+                                       500000.0, interleaved=inter, sec_total=sec)
+                np.testing.assert_allclose(qo[t, h * hd:(h + 1) * hd].cpu().numpy(), exp,
+                                           atol=2e-5, rtol=1e-5)
+            for j in range(nkv):
+                exp = oracle.norm_rope(k[t, j * hd:(j + 1) * hd].cpu().numpy(), kn_h, hd, rd, ps + t,
+                                       500000.0, interleaved=inter, sec_total=sec)
+                gotk = cache.K[ps + t, j * hd:(j + 1) * hd].float().cpu().numpy()
+                np.testing.assert_allclose(gotk, exp.astype(np.float16).astype(np.float32),
+                                           atol=2e-3, rtol=1e-3)
+                gotv = cache.V[ps + t, j * hd:(j + 1) * hd].cpu()
+                assert torch.equal(gotv, v[t, j * hd:(j + 1) * hd].half().cpu())
+    cache.free()
+
+
+def test_step_host_matches_oracle(ab, oracle):
+    """Host-buffer step: RoPE'd K/V append at pos + decode, end to end."""
+    nq, nkv, hd = 32, 8, 128
+    lens = [77, 1000, 1]
+    caches = [ab.KVCache(L + 8, nkv, hd, nq) for L in lens]
+    rng = np.random.RandomState(8)
+    Kf, Vf = [], []
+    for c, L in zip(caches, lens):
+        kr = rng.standard_normal((L, nkv * hd)).astype(np.float32)
+        vr = rng.standard_normal((L, nkv * hd)).astype(np.float32)
+        c.K[:L] = torch.from_numpy(kr).half().cuda()
+        c.V[:L] = torch.from_numpy(vr).half().cuda()
+        Kf.append(kr.astype(np.float16).astype(np.float32))
+        Vf.append(vr.astype(np.float16).astype(np.float32))
+    B = len(lens)
+    q = torch.from_numpy(rng.standard_normal((B, nq * hd)).astype(np.float32)).pin_memory()
+    k = torch.from_numpy(rng.standard_normal((B, nkv * hd)).astype(np.float32)).pin_memory()
+    v = torch.from_numpy(rng.standard_normal((B, nkv * hd)).astype(np.float32)).pin_memory()
+    out = torch.empty(B, nq * hd).pin_memory()
+    ab.step_host([c.handle for c in caches], q, k, v, lens, out, nq, nkv, hd,
+                 rope_dim=hd, rope_base=500000.0)
+    qr = np.stack([oracle.rope_rows(q[b:b + 1].numpy(), nq, hd, [lens[b]], 500000.0)[0] for b in range(B)])
+    for b in range(B):
+        kr = oracle.rope_rows(k[b:b + 1].numpy(), nkv, hd, [lens[b]], 500000.0)[0]
+        Kf[b] = np.concatenate([Kf[b], kr.astype(np.float16).astype(np.float32)[None]])
+        Vf[b] = np.concatenate([Vf[b], v[b:b + 1].numpy().astype(np.float16).astype(np.float32)])
+    ref = oracle.decode_batch(qr, Kf, Vf, lens, nq, nkv, hd)
+    assert_parity(out.numpy(), ref, what="step_host")
+    for c in caches:
+        c.free()
+
+
+def test_argument_errors(ab):
+    q = torch.zeros(1, 32 * 96, device="cuda")
+    t = torch.zeros(1, dtype=torch.int64, device="cuda")
+    p = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with pytest.raises(ab.GPUError) as e:
+        ab.decode(q, t, t, p, 32, 8, 96, max_kv_len=1)       # hd 96 unsupported
+    assert e.value.code == ab.ASPIDA_ERR_UNSUPPORTED
+    with pytest.raises(ab.GPUError) as e:
+        ab.decode(torch.zeros(1, 32 * 128, device="cuda"), t, t, p, 32, 3, 128, max_kv_len=1)
+    assert e.value.code == ab.ASPIDA_ERR_ARG
+    assert ab.last_error() != 0
+    assert ab.last_error() == 0
