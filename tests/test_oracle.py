@@ -41,8 +41,9 @@ def test_rope_matches_reference_kernel(oracle, c):
     ref = _fixture(c["name"])
     use_ff = None if c["ff"] == "ones" else ff
     got = oracle.rope_apply(x, c["base"], c["pos"], ff=use_ff)
-    # large angles (pos * inv_freq up to ~3e4 rad) amplify 1-ulp angle differences
-    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-3 if c["pos"] > 10000 else 2e-5)
+    # theta = pos / base^(2i/d) in f32: a 1-ulp powf difference between CUDA and
+    # libm moves the angle by ~pos * 6e-8 rad, so the bound grows with pos.
+    np.testing.assert_allclose(got, ref, rtol=0, atol=2e-5 + 1.2e-7 * c["pos"] * np.abs(x).max())
 
 
 @pytest.mark.parametrize("c", cases.CHUNK_CASES, ids=lambda c: c["name"])
