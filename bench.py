@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="for ncu: only warm-up + timed decode steps, no clock soak, e2e or CPU legs")
     return ap.parse_args()
 
 
@@ -248,6 +250,12 @@ def main():
         step()
     torch.cuda.synchronize()
 
+    if args.profile:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_run": True, "steps": args.steps}))
+        return
     sampler = ClockSampler(local)
     sampler.start()
     t_end = time.perf_counter() + 1.5        # keep the GPU under load for clock samples

@@ -120,9 +120,12 @@ int aspida_attn_prep(const float* q, const float* k, const float* v, int P, int 
  *   scale    softmax scale (1/sqrt(hd) for Llama/Qwen, 1.0 for Gemma)
  *   window   sliding window (keys max(0,pos-window+1)..pos), 0 = none
  *   softcap  s <- softcap*tanh(s/softcap) after scaling, 0 = none
- *   max_kv_len  upper bound of pos+1 over the batch (sizes the split)
- *   chunk    keys per split (multiple of 64), 0 = automatic
- *   workspace/workspace_bytes  dev scratch >= aspida_attn_decode_workspace_size
+ *   max_kv_len  upper bound of pos+1 over the batch (sizes the grid)
+ *   chunk    0 = automatic (one contiguous range of keys per resident warp);
+ *            > 0 = at least `chunk` keys per warp range (fewer, longer ranges)
+ *   workspace/workspace_bytes  dev scratch (256-byte aligned) of at least
+ *            aspida_attn_decode_workspace_size bytes: per-piece (m, l, o)
+ *            partials of sequences split between warps, unit offsets
  * Supported: hd in {64,128,256}, nq % nkv == 0, nq/nkv <= 8.
  * ------------------------------------------------------------------------ */
 size_t aspida_attn_decode_workspace_size(int B, int nq, int nkv, int hd, int max_kv_len,
