@@ -28,9 +28,11 @@
 //  * Online softmax in the log2 domain (scale folded with log2 e), fp32.
 //  * A segment inside one CTA's range is finished by that CTA; a segment cut
 //    between CTAs leaves one (m, l, o) partial per piece in the workspace
-//    (slot = CTA + segment, unique because ranges are contiguous) and a
+//    (slot = CTA + segment, unique because ranges are contiguous), and a
 //    combine kernel merges them (the log-sum-exp merge of
-//    gpu/fattn_sk.cu:84-97).
+//    gpu/fattn_sk.cu:84-97). The combine is launched as a programmatic
+//    dependent, so its launch overlaps the decode grid and only its merge
+//    work follows it.
 #include <algorithm>
 #include <cmath>
 
@@ -59,7 +61,7 @@ struct DecodeParams {
   float* part_m;        // mode 1: [B][nq]
   float* part_l;
   float* part_o;        // mode 1: [B][nq][hd]
-  int* ws_pref;         // [B+1] unit offsets per sequence
+  int* ws_pref;         // [B+1] unit offsets per sequence (for the combine)
   float* ws_ml;         // [slots][HPC][8][2]  (m in log2 units, l)
   float* ws_o;          // [slots][HPC][8][hd]
   DeviceStatus* status;
@@ -115,6 +117,13 @@ __device__ void build_prefix(const DecodeParams& p, int* pref) {
 
 // First unit of CTA c's range: floor(c * U / C).
 __device__ __forceinline__ long range_start(long c, long U, long C) { return c * U / C; }
+
+// CTA whose range holds unit u: the largest c with range_start(c) <= u.
+__device__ __forceinline__ long owner_of(long u, long U, long C) {
+  long c = u * C / U;
+  while (c + 1 < C && range_start(c + 1, U, C) <= u) ++c;
+  return c;
+}
 
 // Cursor over a CTA's units; caches the current (sequence, head group) segment.
 struct Cursor {
@@ -178,9 +187,15 @@ decode_kernel(const DecodeParams p) {
   const long U = pref[p.B];
   if (blockIdx.x == 0)
     for (int i = threadIdx.x; i <= p.B; i += blockDim.x) p.ws_pref[i] = pref[i];
+  // let the combine grid get scheduled now; it waits for this grid to finish
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+  // Every participating CTA owns at least one unit (piece counting relies on
+  // it): with fewer units than CTAs, the surplus CTAs leave.
+  const long C = min((long)p.nctas, max(U, 1L));
   const long cta = blockIdx.x;
-  const long u_begin = range_start(cta, U, p.nctas), u_end = range_start(cta + 1, U, p.nctas);
+  if (cta >= C) return;
+  const long u_begin = range_start(cta, U, C), u_end = range_start(cta + 1, U, C);
   Cursor cur;
   cur.u = u_begin;
   cur.u_end = u_end;
@@ -322,44 +337,53 @@ decode_kernel(const DecodeParams p) {
       }
       const bool whole = cur.seg_u0 >= u_begin && cur.seg_u1 <= u_end;
       const int h0 = kvh * p.G + qc;
-      if (whole && p.mode == 0) {
+      if (whole) {
         const float inv0 = 1.f / l0, inv1 = 1.f / l1;
-        float* ob = p.out + (long)cur.b * p.nq * HD;
-        const float* gb = p.gate ? p.gate + (long)cur.b * p.nq * HD : nullptr;
+        const long ob = (long)cur.b * p.nq * HD;
 #pragma unroll
         for (int mt = 0; mt < KT; ++mt) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (qc + (j & 1) >= p.G) continue;
             const int dim = mt * 16 + g + (j >> 1) * 8;
-            const long idx = (long)(h0 + (j & 1)) * HD + dim;
-            float v = oacc[mt][j] * ((j & 1) ? inv1 : inv0);
-            if (gb) v *= 1.f / (1.f + expf(-gb[idx]));
-            ob[idx] = v;
+            const long idx = ob + (long)(h0 + (j & 1)) * HD + dim;
+            if (p.mode == 0) {
+              float v = oacc[mt][j] * ((j & 1) ? inv1 : inv0);
+              if (p.gate) v *= 1.f / (1.f + expf(-p.gate[idx]));
+              p.out[idx] = v;
+            } else {
+              p.part_o[idx] = oacc[mt][j];
+            }
+          }
+        }
+        if (p.mode == 1 && g == 0) {
+          if (qc < p.G) {
+            p.part_m[(long)cur.b * p.nq + h0] = m_run[0] * kLn2;
+            p.part_l[(long)cur.b * p.nq + h0] = l0;
+          }
+          if (qc + 1 < p.G) {
+            p.part_m[(long)cur.b * p.nq + h0 + 1] = m_run[1] * kLn2;
+            p.part_l[(long)cur.b * p.nq + h0 + 1] = l1;
           }
         }
       } else {
-        const long slot_id = cta + (long)cur.b * p.ngroups + cur.grp;
-        if (slot_id < p.slots) {
-          float* wo = p.ws_o + (slot_id * HPC + h) * 8 * HD;
-          float* wml = p.ws_ml + (slot_id * HPC + h) * 16;
+        // a piece of a segment split between CTAs: leave its partial
+        const long sid = (cta + (long)cur.b * p.ngroups + cur.grp) * HPC + h;
+        float* wo = p.ws_o + sid * 8 * HD;
+        float* wml = p.ws_ml + sid * 16;
 #pragma unroll
-          for (int mt = 0; mt < KT; ++mt) {
+        for (int mt = 0; mt < KT; ++mt) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int dim = mt * 16 + g + (j >> 1) * 8;
-              wo[(qc + (j & 1)) * HD + dim] = oacc[mt][j];
-            }
+          for (int j = 0; j < 4; ++j) {
+            const int dim = mt * 16 + g + (j >> 1) * 8;
+            wo[(qc + (j & 1)) * HD + dim] = oacc[mt][j];
           }
-          if (g == 0) {
-            wml[qc * 2 + 0] = m_run[0];
-            wml[qc * 2 + 1] = l0;
-            wml[(qc + 1) * 2 + 0] = m_run[1];
-            wml[(qc + 1) * 2 + 1] = l1;
-          }
-        } else if (lane == 0 && p.status) {
-          atomicExch(&p.status->code, 2);
-          p.status->where = 2;
+        }
+        if (g == 0) {
+          wml[qc * 2 + 0] = m_run[0];
+          wml[qc * 2 + 1] = l0;
+          wml[(qc + 1) * 2 + 0] = m_run[1];
+          wml[(qc + 1) * 2 + 1] = l1;
         }
       }
     }
@@ -368,55 +392,90 @@ decode_kernel(const DecodeParams p) {
   }
 }
 
-// CTA whose range holds unit u: the largest c with range_start(c) <= u.
-__device__ __forceinline__ long owner_of(long u, long U, long C) {
-  long c = u * C / U;
-  while (c + 1 < C && range_start(c + 1, U, C) <= u) ++c;
-  return c;
-}
-
-// Merge the pieces of each (sequence, kv head): one CTA per pair, one thread
-// per dim, looping the G query heads of the kv head.
+// Merge the pieces of each split (sequence, kv head) segment, one block per
+// query head: the log-sum-exp merge of gpu/fattn_sk.cu:84-97. The block's
+// warps take every NW-th piece (lanes over dims), then reduce through shared
+// memory. Launched as a programmatic dependent of decode_kernel: the block
+// is scheduled early and waits in griddepcontrol.wait until the decode grid
+// has finished and its writes are visible. Sequences with an empty key range
+// (no units) get zeros (mode 0) or an empty partial (mode 1) here.
 template <int HD>
-__global__ void combine_kernel(const DecodeParams p) {
-  const int b = blockIdx.x, kvh = blockIdx.y, d = threadIdx.x;
+__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
+  constexpr int NW = 4, PER = HD / 32;
+  __shared__ float red_o[NW][HD];
+  __shared__ float red_m[NW], red_l[NW];
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int b = blockIdx.x, kvh = blockIdx.y, gq = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int grp = kvh / p.hpc, h = kvh % p.hpc;
+  const int hq = kvh * p.G + gq;
   const long U = p.ws_pref[p.B];
   const int nu = (p.ws_pref[b + 1] - p.ws_pref[b]) / p.ngroups;
-  const long seg = (long)b * p.ngroups + grp;
-  long ca = 0, cb = -1;
-  if (nu > 0) {
-    const long s0 = p.ws_pref[b] + (long)grp * nu;
-    ca = owner_of(s0, U, p.nctas);
-    cb = owner_of(s0 + nu - 1, U, p.nctas);
-    if (p.mode == 0 && ca == cb) return;  // finished by its CTA
-  }
-  for (int gq = 0; gq < p.G; ++gq) {
-    const int hq = kvh * p.G + gq;
-    float M = -INFINITY;
-    for (long c = ca; c <= cb; ++c)
-      if (c + seg < p.slots) M = fmaxf(M, p.ws_ml[((c + seg) * p.hpc + h) * 16 + gq * 2]);
-    float acc = 0.f, L = 0.f;
-    for (long c = ca; c <= cb; ++c) {
-      const long s = (c + seg) * p.hpc + h;
-      if (c + seg >= p.slots) continue;
-      const float wt = fast_exp2(p.ws_ml[s * 16 + gq * 2] - M);
-      L += wt * p.ws_ml[s * 16 + gq * 2 + 1];
-      acc += wt * p.ws_o[s * 8 * HD + gq * HD + d];
+  const long oi = ((long)b * p.nq + hq) * HD;
+  if (nu == 0) {
+    for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+      if (p.mode == 0) p.out[oi + d] = 0.f;
+      else p.part_o[oi + d] = 0.f;
     }
-    const long oi = ((long)b * p.nq + hq) * HD + d;
-    const bool empty = cb < ca;
-    if (p.mode == 0) {
-      float v = L > 0.f ? acc / L : 0.f;
-      if (p.gate) v *= 1.f / (1.f + expf(-p.gate[oi]));
-      p.out[oi] = v;
+    if (p.mode == 1 && threadIdx.x == 0) {
+      p.part_m[(long)b * p.nq + hq] = kNegBig;
+      p.part_l[(long)b * p.nq + hq] = 0.f;
+    }
+    return;
+  }
+  const long C = min((long)p.nctas, max(U, 1L));
+  const long s0 = p.ws_pref[b] + (long)grp * nu;
+  const long ca = owner_of(s0, U, C), cb = owner_of(s0 + nu - 1, U, C);
+  if (ca == cb) return;  // whole segment: finished by its CTA
+  const long seg = (long)b * p.ngroups + grp;
+
+  float M = -INFINITY;
+  for (long c = ca + threadIdx.x; c <= cb; c += blockDim.x)
+    M = fmaxf(M, p.ws_ml[((c + seg) * p.hpc + h) * 16 + gq * 2]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  if (lane == 0) red_m[warp] = M;
+  __syncthreads();
+  M = fmaxf(fmaxf(red_m[0], red_m[1]), fmaxf(red_m[2], red_m[3]));
+
+  float L = 0.f, acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+#pragma unroll 4
+  for (long c = ca + warp; c <= cb; c += NW) {
+    const long s = (c + seg) * p.hpc + h;
+    const float wt = fast_exp2(p.ws_ml[s * 16 + gq * 2] - M);
+    L += wt * p.ws_ml[s * 16 + gq * 2 + 1];
+    const float* o = p.ws_o + s * 8 * HD + gq * HD + lane * PER;
+    if constexpr (PER == 2) {
+      const float2 t = *reinterpret_cast<const float2*>(o);
+      acc[0] += wt * t.x; acc[1] += wt * t.y;
     } else {
-      p.part_o[oi] = empty ? 0.f : acc;
-      if (d == 0) {
-        p.part_m[(long)b * p.nq + hq] = empty ? kNegBig : M * kLn2;
-        p.part_l[(long)b * p.nq + hq] = empty ? 0.f : L;
+#pragma unroll
+      for (int i = 0; i < PER; i += 4) {
+        const float4 t = *reinterpret_cast<const float4*>(o + i);
+        acc[i] += wt * t.x; acc[i + 1] += wt * t.y; acc[i + 2] += wt * t.z; acc[i + 3] += wt * t.w;
       }
     }
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) red_o[warp][lane * PER + i] = acc[i];
+  if (lane == 0) red_l[warp] = L;
+  __syncthreads();
+  L = red_l[0] + red_l[1] + red_l[2] + red_l[3];
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    const float v = red_o[0][d] + red_o[1][d] + red_o[2][d] + red_o[3][d];
+    if (p.mode == 0) {
+      float r = L > 0.f ? v / L : 0.f;
+      if (p.gate) r *= 1.f / (1.f + expf(-p.gate[oi + d]));
+      p.out[oi + d] = r;
+    } else {
+      p.part_o[oi + d] = v;
+    }
+  }
+  if (p.mode == 1 && threadIdx.x == 0) {
+    p.part_m[(long)b * p.nq + hq] = M * kLn2;
+    p.part_l[(long)b * p.nq + hq] = L;
   }
 }
 
@@ -468,8 +527,20 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
   p.ngroups = p.nkv / HPC;
   kern<<<(int)ctas, Geo::THREADS, smem, st>>>(p);
   ASPIDA_CHECK_LAUNCH();
-  combine_kernel<HD><<<dim3(p.B, p.nkv), HD, 0, st>>>(p);
-  ASPIDA_CHECK_LAUNCH();
+  // the combine is a programmatic dependent: launched now, it runs its
+  // merges as soon as the decode grid completes
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.B, p.nkv, p.G);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaError_t e = cudaLaunchKernelEx(&cfg, combine_kernel<HD>, p); e != cudaSuccess)
+    return record_status((int)e);
   return 0;
 }
 

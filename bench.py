@@ -343,7 +343,7 @@ def main():
                                               + B * (2 * 4 + 2 * 8)),
                     "d2h_bytes_per_step": int(op.numel() * 4),
                     "ms_per_step": round(ms_e2e_max, 5)},
-            "gpu_launches": args.steps * 2,
+            "gpu_launches": args.steps * 2,   # decode_kernel + combine_kernel per step
             "clocks": clocks,
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -124,8 +124,10 @@ int aspida_attn_prep(const float* q, const float* k, const float* v, int P, int 
  *   chunk    0 = automatic (one contiguous range of keys per resident warp);
  *            > 0 = at least `chunk` keys per warp range (fewer, longer ranges)
  *   workspace/workspace_bytes  dev scratch (256-byte aligned) of at least
- *            aspida_attn_decode_workspace_size bytes: per-piece (m, l, o)
- *            partials of sequences split between warps, unit offsets
+ *            aspida_attn_decode_workspace_size bytes: (m, l, o) partials of
+ *            sequences split between CTAs and the unit offsets. No
+ *            initialisation is needed. Calls that share a workspace must not
+ *            overlap on the GPU.
  * Supported: hd in {64,128,256}, nq % nkv == 0, nq/nkv <= 8.
  * ------------------------------------------------------------------------ */
 size_t aspida_attn_decode_workspace_size(int B, int nq, int nkv, int hd, int max_kv_len,
