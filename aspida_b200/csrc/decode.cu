@@ -571,7 +571,7 @@ int run_decode(DecodeParams& p, int hd, int max_kv_len, int chunk, void* ws, siz
   p.ws_ml = reinterpret_cast<float*>(wb + w.ml);
   p.ws_o = reinterpret_cast<float*>(wb + w.o);
   p.slots = w.slots;
-  p.status = device_status_ptr();
+  if (!p.status) p.status = device_status_ptr();
   switch (hd) {
     case 64: return launch_decode_hd<64>(p, units_hint / heads_per_cta(p.nkv, 64), chunk, st);
     case 128: return launch_decode_hd<128>(p, units_hint / heads_per_cta(p.nkv, 128), chunk, st);
@@ -599,6 +599,26 @@ int decode(const float* q, const float* gate, const void* const* K, const void* 
   p.B = B; p.nq = nq; p.nkv = nkv; p.G = nkv > 0 ? nq / nkv : 0;
   p.window = window; p.mode = 0;
   p.scale_log2 = scale * kLog2e; p.softcap = softcap;
+  if (B > 0 && (!pos || !out)) return record_status(ASPIDA_ERR_ARG);
+  return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
+}
+
+// As decode(), with the device status word supplied by the caller instead of
+// the library's lazily allocated one.
+int decode_with_status(const float* q, const float* gate, const void* const* K,
+                       const void* const* V, const int* pos, const int* max_len, float* out,
+                       int B, int nq, int nkv, int hd, float scale, int window, float softcap,
+                       int max_kv_len, int chunk, void* ws, size_t ws_bytes,
+                       DeviceStatus* status, cudaStream_t st) {
+  DecodeParams p{};
+  p.q = q; p.gate = gate;
+  p.K = reinterpret_cast<const __half* const*>(K);
+  p.V = reinterpret_cast<const __half* const*>(V);
+  p.pos = pos; p.max_len = max_len; p.out = out;
+  p.B = B; p.nq = nq; p.nkv = nkv; p.G = nkv > 0 ? nq / nkv : 0;
+  p.window = window; p.mode = 0;
+  p.scale_log2 = scale * kLog2e; p.softcap = softcap;
+  p.status = status;
   if (B > 0 && (!pos || !out)) return record_status(ASPIDA_ERR_ARG);
   return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
 }

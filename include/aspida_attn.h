@@ -170,6 +170,23 @@ int aspida_attn_step_host(const int* handles, int B, const float* q, const float
                           float scale, int window, float softcap, int rd, float base,
                           int interleaved, void* stream);
 
+/* Allocation-free variant of aspida_attn_decode, for callers that cannot
+ * allocate device memory (inside an allocator callback, under a budget
+ * reserved up front, or on a thread that must not block on the device-wide
+ * synchronisation cudaMalloc/cudaFree can imply). No counterpart in the
+ * reference. Same arguments as aspida_attn_decode without the workspace:
+ * its scratch is a 16 MiB array compiled into the library, held on every GPU
+ * that loads it until exit. Returns ASPIDA_ERR_WORKSPACE when
+ * aspida_attn_decode_workspace_size of the call exceeds that (e.g. B > ~360
+ * at nkv 8, hd 128). The first call on each device looks up the array's
+ * device address; make it before any stream capture. All calls share the
+ * array, so calls that overlap on the GPU race: serialise them. */
+int aspida_attn_decode_noalloc(const float* q, const float* gate, const void* const* K,
+                               const void* const* V, const int* pos, const int* max_len,
+                               float* out, int B, int nq, int nkv, int hd, float scale,
+                               int window, float softcap, int max_kv_len, int chunk,
+                               void* stream);
+
 #ifdef __cplusplus
 }
 #endif
