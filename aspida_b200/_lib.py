@@ -37,6 +37,10 @@ SIGNATURES = {
     "aspida_attn_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "aspida_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32,
                                          f32, i32, i32, vp]),
+    "aspida_attn_prefill": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, f32, i32, f32,
+                                  vp]),
+    "aspida_attn_prefill_batch": (i32, [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
+                                        i32, f32, vp]),
     "aspida_attn_step_host": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, f32,
                                     i32, f32, i32, vp]),
 }

@@ -298,3 +298,47 @@ def step_host(handles: Sequence[int], q, k, v, pos, out, nq: int, nkv: int, hd: 
         _stream(stream))
     del pos_arr
     _check(rc, "step_host")
+
+
+def prefill(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, nq: int, nkv: int, hd: int,
+            pos_start: int = 0, *, gate: Optional[torch.Tensor] = None,
+            scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
+            out_dtype=torch.float16, out: Optional[torch.Tensor] = None,
+            stream=None) -> torch.Tensor:
+    """Causal prefill: q fp16 [P, nq*hd] at positions pos_start.., K/V fp16
+    caches [>= pos_start+P, nkv*hd]. Returns [P, nq*hd] in ``out_dtype``."""
+    P = q.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((P, nq * hd), dtype=out_dtype, device=q.device)
+    rc = _lib_().aspida_attn_prefill(
+        _ptr(q), _ptr(K), _ptr(V), _ptr(gate), _ptr(out), int(out.dtype == torch.float32), nq,
+        nkv, hd, P, pos_start, scale, window, softcap, _stream(stream))
+    _check(rc, "prefill")
+    return out
+
+
+def prefill_batch(qs, Ks, Vs, nq: int, nkv: int, hd: int, pos_starts=None, *,
+                  gates=None, outs=None, scale: Optional[float] = None, window: int = 0,
+                  softcap: float = 0.0, out_dtype=torch.float16, stream=None):
+    """Prefill several sequences in one launch (each its own q/K/V/out)."""
+    n = len(qs)
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if pos_starts is None:
+        pos_starts = [0] * n
+    if outs is None:
+        outs = [torch.empty((q.shape[0], nq * hd), dtype=out_dtype, device=q.device) for q in qs]
+    arr = lambda ts: (C.c_void_p * n)(*[None if t is None else t.data_ptr() for t in ts])
+    qa, ka, va, oa = arr(qs), arr(Ks), arr(Vs), arr(outs)
+    ga = arr(gates) if gates is not None else None
+    Pa = (C.c_int * n)(*[q.shape[0] for q in qs])
+    pa = (C.c_int * n)(*pos_starts)
+    rc = _lib_().aspida_attn_prefill_batch(
+        n, C.addressof(qa), C.addressof(ka), C.addressof(va),
+        None if ga is None else C.addressof(ga), C.addressof(oa), C.addressof(Pa),
+        C.addressof(pa), int(outs[0].dtype == torch.float32), nq, nkv, hd, scale, window,
+        softcap, _stream(stream))
+    _check(rc, "prefill_batch")
+    return outs

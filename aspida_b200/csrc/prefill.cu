@@ -1,0 +1,434 @@
+// prefill.cu — causal (optionally sliding-window, softcapped, gated) GQA
+// prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM + TMA).
+//
+// Replaces the shim's prefill attention, aspida_ggml_fattn_prefill
+// (gpu/fattn_ggml.cuh:109-141, ggml fattn-mma) and its unused own variants
+// k_fattn_attend_tile / k_fattn_tile_gqa / k_fattn_wmma[3]
+// (gpu/gpu_matvec.cu:3309-3682). Semantics: P queries at positions
+// pos_start..pos_start+P-1 attend keys max(0, pos-window+1)..pos of the fp16
+// cache; out = softmax(scale * q k^T [softcapped]) v [x sigmoid(gate)].
+//
+// One CTA computes one 128-row query tile of one query head:
+//   warp 0      TMA producer: the Q tile once, then K and V tiles of BN keys
+//               (2D tensor maps, 128-byte swizzle, double-buffered stages).
+//   warp 1      owns TMEM (alloc/dealloc); one elected lane issues the MMAs:
+//               S_j = Q K_j^T (A, B from shared memory, K-major) into one of
+//               two S buffers, then O += P_{j-1} V_{j-1} with P read from TMEM
+//               (the A operand) and V from shared memory (MN-major).
+//   warps 4-7   softmax: thread r owns query row r (TMEM lane r). It loads
+//               S_j, masks (causal / window / length), computes the online
+//               softmax in the log2 domain, writes P_j as fp16 back into the
+//               S_j columns, and rescales O by exp2(m_old - m_new) once
+//               PV_{j-1} has landed (skipped when no row of the warp grew).
+//               The epilogue reads O, divides by l and stores the row.
+// TMEM columns: S0 [0, BN), S1 [BN, 2BN), O [256, 256 + HD); 512 allocated.
+//
+// Every mbarrier wait is bounded; a wait that runs out sets the device
+// status word and the CTA unwinds (TMEM is freed on every path).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "common.cuh"
+#include "tcgen05.cuh"
+
+namespace aspida {
+namespace {
+
+constexpr int BM = 128;
+constexpr int kMaxSeq = 8;            // sequences per launch
+constexpr int kThreads = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct PrefillParams {
+  CUtensorMap qmap[kMaxSeq];
+  CUtensorMap kmap[kMaxSeq];
+  CUtensorMap vmap[kMaxSeq];
+  void* out[kMaxSeq];
+  const float* gate[kMaxSeq];
+  int P[kMaxSeq];
+  int pos_start[kMaxSeq];
+  DeviceStatus* status;
+  int nq, nkv, G, window, out_f32, ntq;
+  float scale_log2, softcap;
+};
+
+template <int HD>
+struct PGeo {
+  static constexpr int BN = HD <= 128 ? 128 : 64;     // keys per KV tile
+  static constexpr int CH = HD / 64;                  // 64-column (128-byte) chunks
+  static constexpr int Q_BYTES = BM * HD * 2;
+  static constexpr int KV_BYTES = BN * HD * 2;        // one K (or V) tile
+  static constexpr int NS = 2;                        // K/V stages
+  static constexpr int SMEM_USED = Q_BYTES + 2 * NS * KV_BYTES;
+  // at least ~116 KB so only one CTA (and one 512-column TMEM allocation) fits per SM
+  static constexpr int SMEM = (SMEM_USED > 118 * 1024 ? SMEM_USED : 118 * 1024) + 1024;
+  static constexpr uint32_t O_COL = 256;
+  static constexpr uint32_t TMEM_COLS = 512;
+};
+
+struct Sync {
+  uint64_t q_full;
+  uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
+  uint64_t s_full[2], p_ready[2];
+  uint64_t o_done, o_final;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sync& sy,
+                                              const PrefillParams& p, int where) {
+  if (sy.abort) return false;
+  if (mbar_wait_bounded(bar, parity)) return true;
+  sy.abort = 1;
+  if (p.status) {
+    atomicExch(&p.status->code, kDevTimeoutMbar);
+    p.status->where = where;
+  }
+  return false;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+prefill_kernel(const __grid_constant__ PrefillParams p) {
+  using Geo = PGeo<HD>;
+  constexpr int BN = Geo::BN, CH = Geo::CH, NS = Geo::NS;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ Sync sy;
+
+  const int seq = blockIdx.z, h = blockIdx.y;
+  const int qt = p.ntq - 1 - (int)blockIdx.x;      // heaviest (latest) tiles first
+  const int P = p.P[seq], ps = p.pos_start[seq];
+  if (qt * BM >= P) return;
+  const int kvh = h / p.G;
+  const int len = ps + P;
+  const int q_first = ps + qt * BM;
+  const int q_last = min(ps + P, q_first + BM) - 1;
+  const int kv_lo = p.window > 0 ? max(0, q_first - p.window + 1) : 0;
+  const int t0 = kv_lo / BN;
+  const int n = q_last / BN - t0 + 1;                 // KV tiles
+
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* Qs = smem;
+  unsigned char* Ks = smem + Geo::Q_BYTES;
+  unsigned char* Vs = Ks + NS * Geo::KV_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&sy.q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sy.k_full[s], 1);
+      mbar_init(&sy.v_full[s], 1);
+      mbar_init(&sy.k_empty[s], 1);
+      mbar_init(&sy.v_empty[s], 1);
+      mbar_init(&sy.s_full[s], 1);
+      mbar_init(&sy.p_ready[s], 128);
+    }
+    mbar_init(&sy.o_done, 1);
+    mbar_init(&sy.o_final, 1);
+    sy.abort = 0;
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sy.tmem_base, Geo::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  fence_mbar_init();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sy.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (tc::elect_one()) {
+      mbar_arrive_expect_tx(&sy.q_full, Geo::Q_BYTES);
+      for (int c = 0; c < CH; ++c)
+        tc::tma_load_2d(Qs + c * BM * 128, &p.qmap[seq], h * HD + c * 64, qt * BM, &sy.q_full);
+      for (int j = 0; j < n; ++j) {
+        const int s = j % NS;
+        const int row = (t0 + j) * BN;
+        if (j >= NS && !wait_or_abort(&sy.k_empty[s], ((j / NS) - 1) & 1, sy, p, 20)) break;
+        mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
+        for (int c = 0; c < CH; ++c)
+          tc::tma_load_2d(Ks + s * Geo::KV_BYTES + c * BN * 128, &p.kmap[seq], kvh * HD + c * 64,
+                          row, &sy.k_full[s]);
+        if (j >= NS && !wait_or_abort(&sy.v_empty[s], ((j / NS) - 1) & 1, sy, p, 21)) break;
+        mbar_arrive_expect_tx(&sy.v_full[s], Geo::KV_BYTES);
+        for (int c = 0; c < CH; ++c)
+          tc::tma_load_2d(Vs + s * Geo::KV_BYTES + c * BN * 128, &p.vmap[seq], kvh * HD + c * 64,
+                          row, &sy.v_full[s]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (tc::elect_one()) {
+      constexpr uint32_t idS = tc::idesc_f16_f32(BM, BN, false, false);
+      constexpr uint32_t idO = tc::idesc_f16_f32(BM, HD, false, true);
+      const uint32_t qbase = smem_u32(Qs), kbase = smem_u32(Ks), vbase = smem_u32(Vs);
+      bool ok = wait_or_abort(&sy.q_full, 0, sy, p, 30);
+      tc::fence_after_sync();
+      for (int j = 0; ok && j <= n; ++j) {
+        if (j < n) {
+          const int s = j % NS;
+          if (!wait_or_abort(&sy.k_full[s], (j / NS) & 1, sy, p, 31)) break;
+          tc::fence_after_sync();
+          const uint32_t sb = tmem + (uint32_t)((j & 1) * BN);
+#pragma unroll
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const int c = kk >> 2;
+            const uint64_t a = tc::smem_desc_sw128(qbase + c * BM * 128 + (kk & 3) * 32, 16, 1024);
+            const uint64_t b = tc::smem_desc_sw128(
+                kbase + s * Geo::KV_BYTES + c * BN * 128 + (kk & 3) * 32, 16, 1024);
+            tc::mma_ss(sb, a, b, idS, kk > 0);
+          }
+          tc::commit(&sy.s_full[j & 1]);
+          tc::commit(&sy.k_empty[s]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, s = jj % NS;
+          if (!wait_or_abort(&sy.p_ready[jj & 1], (jj >> 1) & 1, sy, p, 32)) break;
+          if (!wait_or_abort(&sy.v_full[s], (jj / NS) & 1, sy, p, 33)) break;
+          tc::fence_after_sync();
+          const uint32_t pb = tmem + (uint32_t)((jj & 1) * BN);
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const uint64_t b = tc::smem_desc_sw128(vbase + s * Geo::KV_BYTES + kk * 16 * 128,
+                                                   BN * 128, 1024);
+            tc::mma_ts(tmem + Geo::O_COL, pb + kk * 8, b, idO, (jj > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::commit(&sy.v_empty[s]);
+          tc::commit(&sy.o_done);
+        }
+      }
+      tc::commit(&sy.o_final);   // fires once every MMA issued above has completed
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------ softmax / epilogue ------------------------
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;                    // query row == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+    const int qpos = q_first + r;
+    const int win_lo = p.window > 0 ? qpos - p.window + 1 : 0;
+    float m_run = -INFINITY, l_run = 0.f;
+    float s[BN];
+    for (int j = 0; j < n; ++j) {
+      if (!wait_or_abort(&sy.s_full[j & 1], (j >> 1) & 1, sy, p, 40)) break;
+      tc::fence_after_sync();
+      const uint32_t sb = tmem + lane_addr + (uint32_t)((j & 1) * BN);
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tc::tmem_ld32(sb + c * 32, s + c * 32);
+      tc::tmem_wait_ld();
+      const int key0 = (t0 + j) * BN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const int key = key0 + i;
+        float x = s[i];
+        if (p.softcap > 0.f) x = p.softcap * tanhf(x * (p.scale_log2 / kLog2e) / p.softcap) * kLog2e;
+        else x *= p.scale_log2;
+        const bool valid = key <= qpos && key >= win_lo && key < len;
+        x = valid ? x : -INFINITY;
+        s[i] = x;
+        mx = fmaxf(mx, x);
+      }
+      const float m_new = fmaxf(m_run, mx);
+      const float m_use = m_new == -INFINITY ? 0.f : m_new;
+      const float corr = fast_exp2(m_run - m_use);
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 64; ++c) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float a = fast_exp2(s[c * 64 + 2 * i] - m_use);
+          const float b = fast_exp2(s[c * 64 + 2 * i + 1] - m_use);
+          sum += a + b;
+          pk[i] = pack_half2(a, b);
+        }
+        tc::tmem_st32(sb + c * 32, pk);
+      }
+      l_run = l_run * corr + sum;
+      m_run = m_new;
+      if (j >= 1) {
+        // O holds tiles < j at the previous max: rescale once PV_{j-1} landed
+        if (!wait_or_abort(&sy.o_done, (j - 1) & 1, sy, p, 41)) break;
+        tc::fence_after_sync();
+        if (__any_sync(0xffffffffu, corr != 1.f)) {
+          const uint32_t ob = tmem + lane_addr + Geo::O_COL;
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            float o[32];
+            tc::tmem_ld32(ob + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tc::tmem_st32(ob + c * 32, reinterpret_cast<const uint32_t*>(o));
+          }
+        }
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&sy.p_ready[j & 1]);
+    }
+    if (wait_or_abort(&sy.o_final, 0, sy, p, 42)) {
+      tc::fence_after_sync();
+      const int row = qt * BM + r;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const long obase = ((long)row * p.nq + h) * HD;
+      const float* g = p.gate[seq];
+      const uint32_t ob = tmem + lane_addr + Geo::O_COL;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tc::tmem_ld32(ob + c * 32, o);
+        tc::tmem_wait_ld();
+        if (row < P) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            o[i] *= inv;
+            if (g) o[i] *= 1.f / (1.f + expf(-g[obase + c * 32 + i]));
+          }
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out[seq]) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out[seq]) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pack_half2(o[8 * i], o[8 * i + 1]), pack_half2(o[8 * i + 2], o[8 * i + 3]),
+                                  pack_half2(o[8 * i + 4], o[8 * i + 5]), pack_half2(o[8 * i + 6], o[8 * i + 7]));
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, Geo::TMEM_COLS);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2D fp16 map over [rows][cols] (row stride cols*2 bytes), box 64 x box_rows,
+// 128-byte swizzle, zero fill out of bounds.
+bool make_map(CUtensorMap* m, const void* base, long cols, long rows, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int HD>
+int launch_prefill(PrefillParams& p, int nseq, cudaStream_t st) {
+  using Geo = PGeo<HD>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
+    if (e != cudaSuccess) return record_status((int)e);
+    configured[dev] = true;
+  }
+  dim3 grid(p.ntq, p.nq, nseq);
+  prefill_kernel<HD><<<grid, kThreads, Geo::SMEM, st>>>(p);
+  ASPIDA_CHECK_LAUNCH();
+  return 0;
+}
+
+}  // namespace
+
+int prefill_batch(int nseq, const void* const* q, const void* const* K, const void* const* V,
+                  const float* const* gate, void* const* out, const int* P, const int* pos_start,
+                  int out_f32, int nq, int nkv, int hd, float scale, int window, float softcap,
+                  cudaStream_t st) {
+  if (nseq <= 0) return 0;
+  if (!q || !K || !V || !out || !P || !pos_start || nq <= 0 || nkv <= 0 || nq % nkv)
+    return record_status(ASPIDA_ERR_ARG);
+  if (hd != 64 && hd != 128 && hd != 256) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  for (int base = 0; base < nseq; base += kMaxSeq) {
+    const int cnt = std::min(kMaxSeq, nseq - base);
+    PrefillParams p;
+    memset(&p, 0, sizeof(p));
+    int maxP = 0;
+    const int box_kv = hd <= 128 ? 128 : 64;
+    for (int i = 0; i < cnt; ++i) {
+      const int s = base + i;
+      if (P[s] < 0 || pos_start[s] < 0 || !q[s] || !K[s] || !V[s] || !out[s])
+        return record_status(ASPIDA_ERR_ARG);
+      if (((uintptr_t)q[s] | (uintptr_t)K[s] | (uintptr_t)V[s] | (uintptr_t)out[s]) & 15)
+        return record_status(ASPIDA_ERR_ARG);
+      const int Pv = std::max(P[s], 1), len = pos_start[s] + Pv;
+      if (!make_map(&p.qmap[i], q[s], (long)nq * hd, Pv, BM) ||
+          !make_map(&p.kmap[i], K[s], (long)nkv * hd, len, box_kv) ||
+          !make_map(&p.vmap[i], V[s], (long)nkv * hd, len, box_kv))
+        return record_status(ASPIDA_ERR_ARG);
+      p.out[i] = out[s];
+      p.gate[i] = gate ? gate[s] : nullptr;
+      p.P[i] = P[s];
+      p.pos_start[i] = pos_start[s];
+      maxP = std::max(maxP, P[s]);
+    }
+    if (maxP == 0) continue;
+    p.status = device_status_ptr();
+    p.nq = nq; p.nkv = nkv; p.G = nq / nkv;
+    p.window = window; p.out_f32 = out_f32;
+    p.ntq = (maxP + BM - 1) / BM;
+    p.scale_log2 = scale * kLog2e;
+    p.softcap = softcap;
+    int rc = hd == 64 ? launch_prefill<64>(p, cnt, st)
+           : hd == 128 ? launch_prefill<128>(p, cnt, st)
+                       : launch_prefill<256>(p, cnt, st);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+}  // namespace aspida
+
+extern "C" int aspida_attn_prefill(const void* q, const void* K, const void* V, const float* gate,
+                                   void* out, int out_f32, int nq, int nkv, int hd, int P,
+                                   int pos_start, float scale, int window, float softcap,
+                                   void* stream) {
+  return aspida::prefill_batch(1, &q, &K, &V, gate ? &gate : nullptr, &out, &P, &pos_start,
+                               out_f32, nq, nkv, hd, scale, window, softcap,
+                               (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_prefill_batch(int nseq, const void* const* q, const void* const* K,
+                                         const void* const* V, const float* const* gate,
+                                         void* const* out, const int* P, const int* pos_start,
+                                         int out_f32, int nq, int nkv, int hd, float scale,
+                                         int window, float softcap, void* stream) {
+  return aspida::prefill_batch(nseq, q, K, V, gate, out, P, pos_start, out_f32, nq, nkv, hd, scale,
+                               window, softcap, (cudaStream_t)stream);
+}

@@ -157,6 +157,28 @@ int aspida_attn_decode_partial(const float* q, const void* const* K, const void*
 int aspida_attn_merge(const float* m, const float* l, const float* o, const float* gate,
                       float* out, int S, int rows, int hd, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Causal prefill attention on the tcgen05 tensor cores.
+ * Replaces aspida_ggml_fattn_prefill (gpu/fattn_ggml.cuh:109-141) and the
+ * shim's own prefill kernels (gpu/gpu_matvec.cu:3309-3682).
+ *   q      dev fp16 [P][nq*hd]   roped queries (aspida_attn_prep, q_out_fp16)
+ *   K, V   dev fp16 caches with >= pos_start+P rows of nkv*hd halves
+ *   gate   dev f32 [P][nq*hd] or NULL (out *= sigmoid(gate))
+ *   out    dev [P][nq*hd], fp16 (out_f32 = 0) or f32 (out_f32 = 1)
+ *   query t (position pos_start+t) attends keys max(0, pos-window+1)..pos;
+ *   scale / window / softcap as for decode.
+ * All pointers 16-byte aligned. Supported: hd in {64, 128, 256}. */
+int aspida_attn_prefill(const void* q, const void* K, const void* V, const float* gate, void* out,
+                        int out_f32, int nq, int nkv, int hd, int P, int pos_start, float scale,
+                        int window, float softcap, void* stream);
+
+/* Batched form: nseq sequences, each with its own q/K/V/gate/out pointers
+ * and P / pos_start (host arrays of device pointers and host ints). */
+int aspida_attn_prefill_batch(int nseq, const void* const* q, const void* const* K,
+                              const void* const* V, const float* const* gate, void* const* out,
+                              const int* P, const int* pos_start, int out_f32, int nq, int nkv,
+                              int hd, float scale, int window, float softcap, void* stream);
+
 /* Host-buffer decode step for B resident states — the attention half of
  * aspida_gpu_fattn_step / chain_forward_batch (gpu/gpu_matvec.cu:1613, 2783)
  * without the projections: copies q/k/v/pos from host, runs prep (RoPE, no

@@ -1,0 +1,89 @@
+"""GPU parity of the tcgen05 prefill kernel against the CPU oracle, through
+the C ABI (aspida_attn_prefill / _batch). Tolerance as for decode (max-abs
+2e-3, rel-L2 1e-3); inputs are fp16 on both sides."""
+import numpy as np
+import pytest
+import torch
+
+from tests.util import assert_parity
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def ab():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import aspida_b200
+    return aspida_b200
+
+
+def make(P, ps, nq, nkv, hd, seed, qscale=1.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    q = (torch.randn(P, nq * hd, generator=g, device="cuda") * qscale).half()
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    return q, K, V
+
+
+def oracle_prefill(oracle, q, K, V, ps, nq, nkv, hd, **kw):
+    return oracle.prefill(q.float().cpu().numpy(), K.float().cpu().numpy(),
+                          V.float().cpu().numpy(), ps, nq, nkv, hd, **kw)
+
+
+@pytest.mark.parametrize("hd,nq,nkv,P,ps", [
+    (128, 8, 2, 128, 0), (128, 8, 2, 300, 0), (128, 4, 4, 77, 0), (128, 32, 8, 256, 1000),
+    (64, 8, 2, 200, 37), (64, 4, 1, 129, 0), (256, 4, 2, 150, 10), (256, 16, 8, 130, 64),
+])
+def test_prefill_shapes(ab, oracle, hd, nq, nkv, P, ps):
+    q, K, V = make(P, ps, nq, nkv, hd, seed=hd + P)
+    got = ab.prefill(q, K, V, nq, nkv, hd, ps, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    ref = oracle_prefill(oracle, q, K, V, ps, nq, nkv, hd)
+    assert_parity(got.cpu().numpy(), ref, what=f"hd{hd} {nq}/{nkv} P{P} ps{ps}")
+
+
+def test_prefill_fp16_out_gate_window_softcap(ab, oracle):
+    nq, nkv, hd, P, ps = 16, 8, 256, 300, 100
+    q, K, V = make(P, ps, nq, nkv, hd, seed=5, qscale=0.25)
+    gate = torch.randn(P, nq * hd, device="cuda")
+    for scale, window, cap, g, dt in [(1 / 16, 128, 50.0, None, torch.float32),
+                                      (1.0, 200, 50.0, None, torch.float32),
+                                      (1 / 16, 0, 0.0, gate, torch.float16),
+                                      (1 / 16, 1, 0.0, None, torch.float32)]:
+        got = ab.prefill(q, K, V, nq, nkv, hd, ps, gate=g, scale=scale, window=window,
+                         softcap=cap, out_dtype=dt)
+        torch.cuda.synchronize()
+        ref = oracle_prefill(oracle, q, K, V, ps, nq, nkv, hd, scale=scale, window=window,
+                             softcap=cap, gate=None if g is None else g.cpu().numpy())
+        tol = 2e-3 if dt == torch.float32 else 4e-3   # fp16 output rounding adds <= 2^-11 |o|
+        assert_parity(got.float().cpu().numpy(), ref, max_abs=tol,
+                      what=f"scale {scale} window {window} cap {cap} {dt}")
+
+
+def test_prefill_equals_decode_last_row(ab, oracle):
+    """incremental == batched (tests/test_fullattn.adb:122-144): the last
+    prefill row equals a decode step at that position."""
+    nq, nkv, hd, P = 32, 8, 128, 700
+    q, K, V = make(P, 0, nq, nkv, hd, seed=9)
+    pre = ab.prefill(q, K, V, nq, nkv, hd, 0, out_dtype=torch.float32)
+    dec = ab.decode(q[-1:].float(), ab.ptr_table([K], q.device), ab.ptr_table([V], q.device),
+                    torch.tensor([P - 1], dtype=torch.int32, device="cuda"), nq, nkv, hd,
+                    max_kv_len=P)
+    torch.cuda.synchronize()
+    assert_parity(pre[-1:].cpu().numpy(), dec.cpu().numpy(), what="prefill vs decode")
+
+
+def test_prefill_batch_cfg3_rows(ab, oracle):
+    """BASELINE config 3 (4 x 4096, 32/8, hd128), checked on a seeded row
+    subset: the last 128 rows and every 97th row of each sequence."""
+    nq, nkv, hd, S = 32, 8, 128, 4096
+    qs, Ks, Vs = zip(*[make(S, 0, nq, nkv, hd, seed=30 + b) for b in range(4)])
+    outs = ab.prefill_batch(list(qs), list(Ks), list(Vs), nq, nkv, hd, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    rows = sorted(set(list(range(S - 128, S)) + list(range(0, S, 97))))
+    for b in range(4):
+        ref = oracle_prefill(oracle, qs[b], Ks[b], Vs[b], 0, nq, nkv, hd, rows=rows)
+        assert_parity(outs[b].cpu().numpy()[rows], ref[rows], what=f"cfg3 seq {b}")
