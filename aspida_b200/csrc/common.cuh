@@ -71,11 +71,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: spins with a growing back-off; returns false when the limit
-// (~2^22 polls, on the order of seconds) is exhausted.
+// Bounded wait: polls try_wait (which itself suspends briefly in hardware)
+// without sleeping for the first 2^16 polls, so hand-offs on a busy pipeline
+// cost no added latency; then backs off with __nanosleep. Returns false when
+// the limit (on the order of seconds) is exhausted.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint32_t ns = 32;
+  for (uint32_t it = 0; it < (1u << 16); ++it)
+    if (mbar_try_wait(bar, parity)) return true;
+  uint32_t ns = 64;
   for (uint32_t it = 0; it < (1u << 22); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     __nanosleep(ns);

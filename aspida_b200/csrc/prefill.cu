@@ -43,6 +43,16 @@ constexpr int kMaxSeq = 8;            // sequences per launch
 constexpr int kThreads = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
+#ifdef ASPIDA_TRACE
+// Opt-in timeline (debug builds only): per CTA (first 4), event x tile, clock64.
+__device__ long long g_trace[4][16][64];
+#define TRACE(ev, j) do { if (blockIdx.x + blockIdx.y * gridDim.x + blockIdx.z == 0 || \
+    (blockIdx.y == 0 && blockIdx.z == 0 && blockIdx.x < 4)) \
+    if ((j) < 64) g_trace[blockIdx.x & 3][ev][j] = clock64(); } while (0)
+#else
+#define TRACE(ev, j) do {} while (0)
+#endif
+
 struct PrefillParams {
   CUtensorMap qmap[kMaxSeq];
   CUtensorMap kmap[kMaxSeq];
@@ -89,6 +99,30 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, Sy
     p.status->where = where;
   }
   return false;
+}
+
+// Scores in the log2 domain: s*scale*log2e, or softcap*tanh(s*scale/softcap)
+// *log2e. The branch is taken once per 32-column chunk, outside the element
+// loop, so the uncapped path carries no tanh.
+__device__ __forceinline__ void scores_log2(float* x, bool capped, float cap, float scale_log2) {
+  if (capped) {
+    const float sc = scale_log2 / kLog2e / cap;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] = cap * tanhf(x[i] * sc) * kLog2e;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] *= scale_log2;
+  }
+}
+
+// -inf outside keys max(0, qpos-window+1)..qpos and beyond the length.
+__device__ __forceinline__ void mask_chunk(float* x, int key0, int qpos, int win_lo, int len) {
+  const int hi = min(qpos, len - 1);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const int key = key0 + i;
+    x[i] = (key <= hi && key >= win_lo) ? x[i] : -INFINITY;
+  }
 }
 
 template <int HD>
@@ -152,6 +186,7 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
         const int s = j % NS;
         const int row = (t0 + j) * BN;
         if (j >= NS && !wait_or_abort(&sy.k_empty[s], ((j / NS) - 1) & 1, sy, p, 20)) break;
+        TRACE(0, j);
         mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
         for (int c = 0; c < CH; ++c)
           tc::tma_load_2d(Ks + s * Geo::KV_BYTES + c * BN * 128, &p.kmap[seq], kvh * HD + c * 64,
@@ -176,6 +211,7 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
         if (j < n) {
           const int s = j % NS;
           if (!wait_or_abort(&sy.k_full[s], (j / NS) & 1, sy, p, 31)) break;
+          TRACE(1, j);
           tc::fence_after_sync();
           const uint32_t sb = tmem + (uint32_t)((j & 1) * BN);
 #pragma unroll
@@ -192,7 +228,9 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
         if (j >= 1) {
           const int jj = j - 1, s = jj % NS;
           if (!wait_or_abort(&sy.p_ready[jj & 1], (jj >> 1) & 1, sy, p, 32)) break;
+          TRACE(2, jj);
           if (!wait_or_abort(&sy.v_full[s], (jj / NS) & 1, sy, p, 33)) break;
+          TRACE(3, jj);
           tc::fence_after_sync();
           const uint32_t pb = tmem + (uint32_t)((jj & 1) * BN);
 #pragma unroll
@@ -215,49 +253,58 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
     const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
     const int qpos = q_first + r;
     const int win_lo = p.window > 0 ? qpos - p.window + 1 : 0;
+    const bool capped = p.softcap > 0.f;
     float m_run = -INFINITY, l_run = 0.f;
-    float s[BN];
     for (int j = 0; j < n; ++j) {
       if (!wait_or_abort(&sy.s_full[j & 1], (j >> 1) & 1, sy, p, 40)) break;
+      if (r == 0) TRACE(4, j);
       tc::fence_after_sync();
       const uint32_t sb = tmem + lane_addr + (uint32_t)((j & 1) * BN);
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tc::tmem_ld32(sb + c * 32, s + c * 32);
-      tc::tmem_wait_ld();
       const int key0 = (t0 + j) * BN;
+      // rows whose tile lies wholly inside their causal / window / length
+      // range skip the per-element mask
+      const bool masked = !(key0 + BN - 1 <= qpos && key0 >= win_lo && key0 + BN <= len);
+      // pass 1: scaled (softcapped) scores, row max
       float mx = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float x[32];
+        tc::tmem_ld32(sb + c * 32, x);
+        tc::tmem_wait_ld();
+        scores_log2(x, capped, p.softcap, p.scale_log2);
+        if (masked) mask_chunk(x, key0 + c * 32, qpos, win_lo, len);
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const int key = key0 + i;
-        float x = s[i];
-        if (p.softcap > 0.f) x = p.softcap * tanhf(x * (p.scale_log2 / kLog2e) / p.softcap) * kLog2e;
-        else x *= p.scale_log2;
-        const bool valid = key <= qpos && key >= win_lo && key < len;
-        x = valid ? x : -INFINITY;
-        s[i] = x;
-        mx = fmaxf(mx, x);
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, x[i]);
       }
       const float m_new = fmaxf(m_run, mx);
       const float m_use = m_new == -INFINITY ? 0.f : m_new;
       const float corr = fast_exp2(m_run - m_use);
+      // pass 2: P = exp2(s - m) as fp16 pairs into the first BN/2 columns
       float sum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        float x[32];
+        tc::tmem_ld32(sb + c * 32, x);
+        tc::tmem_wait_ld();
+        scores_log2(x, capped, p.softcap, p.scale_log2);
+        if (masked) mask_chunk(x, key0 + c * 32, qpos, win_lo, len);
+        uint32_t pk[16];
 #pragma unroll
-      for (int c = 0; c < BN / 64; ++c) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float a = fast_exp2(s[c * 64 + 2 * i] - m_use);
-          const float b = fast_exp2(s[c * 64 + 2 * i + 1] - m_use);
-          sum += a + b;
-          pk[i] = pack_half2(a, b);
+        for (int i = 0; i < 16; ++i) {
+          const float e0 = fast_exp2(x[2 * i] - m_use), e1 = fast_exp2(x[2 * i + 1] - m_use);
+          sum += e0 + e1;
+          pk[i] = pack_half2(e0, e1);
         }
-        tc::tmem_st32(sb + c * 32, pk);
+        // P columns c*16.. overwrite S columns already read (<= c*32+31)
+        tc::tmem_st16(sb + c * 16, pk);
       }
       l_run = l_run * corr + sum;
       m_run = m_new;
+      if (r == 0) TRACE(5, j);
       if (j >= 1) {
         // O holds tiles < j at the previous max: rescale once PV_{j-1} landed
         if (!wait_or_abort(&sy.o_done, (j - 1) & 1, sy, p, 41)) break;
+        if (r == 0) TRACE(6, j);
         tc::fence_after_sync();
         if (__any_sync(0xffffffffu, corr != 1.f)) {
           const uint32_t ob = tmem + lane_addr + Geo::O_COL;
@@ -275,6 +322,7 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
       tc::tmem_wait_st();
       tc::fence_before_sync();
       mbar_arrive(&sy.p_ready[j & 1]);
+      if (r == 0) TRACE(7, j);
     }
     if (wait_or_abort(&sy.o_final, 0, sy, p, 42)) {
       tc::fence_after_sync();
