@@ -365,6 +365,312 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Two query tiles per CTA (hd <= 128): rows A = [256*qt, +128) and
+// B = [256*qt + 128, +128) of one head share every K/V tile. Two softmax
+// warpgroups (warps 2-5 for A, 6-9 for B) ping-pong against the MMA issuer:
+// while one warpgroup turns S into P, the tensor core runs the other tile's
+// PV and next S. TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B
+// [384,512). MMAs from one thread complete in issue order, so the commit
+// that signals S_X(j) also certifies PV_X(j-1): the softmax may rescale O_X
+// right after S_X(j) lands. O is only rescaled when some row's max grew by
+// more than 2^8 (log2 domain 8): otherwise the stale max is kept, P <= 2^8
+// fits fp16, and the final 1/l uses the same max.
+// ---------------------------------------------------------------------------
+constexpr int kThreads2 = 320;
+constexpr float kRescaleThreshold = 8.f;
+
+template <int HD>
+struct PGeo2 {
+  static constexpr int BN = 128;
+  static constexpr int CH = HD / 64;
+  static constexpr int QT_BYTES = BM * HD * 2;         // one 128-row Q tile
+  static constexpr int KV_BYTES = BN * HD * 2;
+  static constexpr int NS = 2;
+  static constexpr int SMEM_USED = 2 * QT_BYTES + 2 * NS * KV_BYTES;
+  static constexpr int SMEM = (SMEM_USED > 118 * 1024 ? SMEM_USED : 118 * 1024) + 1024;
+};
+
+struct Sync2 {
+  uint64_t q_full;
+  uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
+  uint64_t s_full[2], p_ready[2];   // per query tile
+  uint64_t o_final;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ bool wait2(uint64_t* bar, uint32_t parity, Sync2& sy,
+                                      const PrefillParams& p, int where) {
+  if (sy.abort) return false;
+  if (mbar_wait_bounded(bar, parity)) return true;
+  sy.abort = 1;
+  if (p.status) {
+    atomicExch(&p.status->code, kDevTimeoutMbar);
+    p.status->where = where;
+  }
+  return false;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kThreads2, 1)
+prefill2_kernel(const __grid_constant__ PrefillParams p) {
+  using Geo = PGeo2<HD>;
+  constexpr int BN = Geo::BN, CH = Geo::CH, NS = Geo::NS;
+  extern __shared__ unsigned char smem_raw[];
+  __shared__ Sync2 sy;
+
+  const int seq = blockIdx.z, h = blockIdx.y;
+  const int qt = p.ntq - 1 - (int)blockIdx.x;        // 256-row tile, heaviest first
+  const int P = p.P[seq], ps = p.pos_start[seq];
+  if (qt * 2 * BM >= P) return;
+  const int kvh = h / p.G;
+  const int len = ps + P;
+  // per query tile X: first/last position and active KV tile range [x0, x1)
+  int qf[2], x0[2], x1[2];
+  for (int X = 0; X < 2; ++X) {
+    const int r0 = qt * 2 * BM + X * BM;
+    qf[X] = ps + r0;
+    if (r0 >= P) { x0[X] = x1[X] = 0; continue; }
+    const int ql = min(ps + P, qf[X] + BM) - 1;
+    const int lo = p.window > 0 ? max(0, qf[X] - p.window + 1) : 0;
+    x0[X] = lo / BN;
+    x1[X] = ql / BN + 1;
+  }
+  const int t0 = x0[0];
+  const int n = max(x1[0], x1[1]) - t0;               // union of KV tiles
+  auto act = [&](int X, int j) { return t0 + j >= x0[X] && t0 + j < x1[X]; };
+
+  unsigned char* smem = reinterpret_cast<unsigned char*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* Qs = smem;                            // [2 tiles][CH][128][64]
+  unsigned char* Ks = smem + 2 * Geo::QT_BYTES;
+  unsigned char* Vs = Ks + NS * Geo::KV_BYTES;
+
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    mbar_init(&sy.q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&sy.k_full[s], 1);
+      mbar_init(&sy.v_full[s], 1);
+      mbar_init(&sy.k_empty[s], 1);
+      mbar_init(&sy.v_empty[s], 1);
+      mbar_init(&sy.s_full[s], 1);
+      mbar_init(&sy.p_ready[s], 128);
+    }
+    mbar_init(&sy.o_final, 1);
+    sy.abort = 0;
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(&sy.tmem_base, 512);
+    tc::tmem_relinquish();
+  }
+  fence_mbar_init();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sy.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (tc::elect_one()) {
+      const int nqt = x1[1] > x0[1] ? 2 : 1;           // tile B may lie past P
+      mbar_arrive_expect_tx(&sy.q_full, nqt * Geo::QT_BYTES);
+      for (int X = 0; X < nqt; ++X)
+        for (int c = 0; c < CH; ++c)
+          tc::tma_load_2d(Qs + X * Geo::QT_BYTES + c * BM * 128, &p.qmap[seq], h * HD + c * 64,
+                          qt * 2 * BM + X * BM, &sy.q_full);
+      for (int j = 0; j < n; ++j) {
+        const int s = j % NS, row = (t0 + j) * BN;
+        if (j >= NS && !wait2(&sy.k_empty[s], ((j / NS) - 1) & 1, sy, p, 20)) break;
+        mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
+        for (int c = 0; c < CH; ++c)
+          tc::tma_load_2d(Ks + s * Geo::KV_BYTES + c * BN * 128, &p.kmap[seq], kvh * HD + c * 64,
+                          row, &sy.k_full[s]);
+        if (j >= NS && !wait2(&sy.v_empty[s], ((j / NS) - 1) & 1, sy, p, 21)) break;
+        mbar_arrive_expect_tx(&sy.v_full[s], Geo::KV_BYTES);
+        for (int c = 0; c < CH; ++c)
+          tc::tma_load_2d(Vs + s * Geo::KV_BYTES + c * BN * 128, &p.vmap[seq], kvh * HD + c * 64,
+                          row, &sy.v_full[s]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer --------------------------------
+    if (tc::elect_one()) {
+      constexpr uint32_t idS = tc::idesc_f16_f32(BM, BN, false, false);
+      constexpr uint32_t idO = tc::idesc_f16_f32(BM, HD, false, true);
+      const uint32_t qbase = smem_u32(Qs), kbase = smem_u32(Ks), vbase = smem_u32(Vs);
+      int np[2] = {0, 0};                              // P tiles consumed per query tile
+      auto issue_S = [&](int X, int j) {
+        const int s = j % NS;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int c = kk >> 2;
+          const uint64_t a = tc::smem_desc_sw128(
+              qbase + X * Geo::QT_BYTES + c * BM * 128 + (kk & 3) * 32, 16, 1024);
+          const uint64_t b = tc::smem_desc_sw128(
+              kbase + s * Geo::KV_BYTES + c * BN * 128 + (kk & 3) * 32, 16, 1024);
+          tc::mma_ss(tmem + X * 128, a, b, idS, kk > 0);
+        }
+        tc::commit(&sy.s_full[X]);
+      };
+      auto issue_PV = [&](int X, int j, bool first) {
+        const int s = j % NS;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const uint64_t b = tc::smem_desc_sw128(vbase + s * Geo::KV_BYTES + kk * 16 * 128,
+                                                 BN * 128, 1024);
+          tc::mma_ts(tmem + 256 + X * 128, tmem + X * 128 + kk * 8, b, idO,
+                     (!first || kk > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = wait2(&sy.q_full, 0, sy, p, 30);
+      tc::fence_after_sync();
+      if (ok && n > 0) {
+        ok = wait2(&sy.k_full[0], 0, sy, p, 31);
+        tc::fence_after_sync();
+        if (ok) {
+          if (act(0, 0)) issue_S(0, 0);
+          if (act(1, 0)) issue_S(1, 0);
+          tc::commit(&sy.k_empty[0]);
+        }
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const int s = j % NS;
+        if (!(ok = wait2(&sy.v_full[s], (j / NS) & 1, sy, p, 33))) break;
+        const bool more = j + 1 < n;
+        if (more) {
+          if (!(ok = wait2(&sy.k_full[(j + 1) % NS], ((j + 1) / NS) & 1, sy, p, 31))) break;
+        }
+        tc::fence_after_sync();
+        for (int X = 0; X < 2; ++X) {
+          if (act(X, j)) {
+            if (!(ok = wait2(&sy.p_ready[X], np[X] & 1, sy, p, 32))) break;
+            tc::fence_after_sync();
+            issue_PV(X, j, np[X] == 0);
+            ++np[X];
+          }
+          if (more && act(X, j + 1)) issue_S(X, j + 1);
+        }
+        if (!ok) break;
+        if (more) tc::commit(&sy.k_empty[(j + 1) % NS]);
+        tc::commit(&sy.v_empty[s]);
+      }
+      tc::commit(&sy.o_final);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ softmax / epilogue ------------------------
+    const int X = warp < 6 ? 0 : 1;                   // query tile of this warpgroup
+    const int lane = threadIdx.x & 31;
+    const int wq = warp & 3;
+    const int r = wq * 32 + lane;                     // row in tile == TMEM lane
+    const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
+    const uint32_t sb = tmem + lane_addr + X * 128;
+    const uint32_t ob = tmem + lane_addr + 256 + X * 128;
+    const int qpos = qf[X] + r;
+    const int win_lo = p.window > 0 ? qpos - p.window + 1 : 0;
+    const bool capped = p.softcap > 0.f;
+    float m_run = -INFINITY, l_run = 0.f;
+    int k = 0;
+    for (int t = x0[X]; t < x1[X]; ++t, ++k) {
+      if (!wait2(&sy.s_full[X], k & 1, sy, p, 40)) break;
+      tc::fence_after_sync();
+      const int key0 = t * BN;
+      const bool masked = !(key0 + BN - 1 <= qpos && key0 >= win_lo && key0 + BN <= len);
+      float s[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tc::tmem_ld32(sb + c * 32, s + c * 32);
+      tc::tmem_wait_ld();
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        scores_log2(s + c * 32, capped, p.softcap, p.scale_log2);
+        if (masked) mask_chunk(s + c * 32, key0 + c * 32, qpos, win_lo, len);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, s[c * 32 + i]);
+      }
+      // keep the stale max unless some row of this warp grew by > 2^8
+      const bool grow = __any_sync(0xffffffffu, mx > m_run + kRescaleThreshold);
+      float corr = 1.f;
+      if (grow) {
+        const float m_new = fmaxf(m_run, mx);
+        corr = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
+        m_run = m_new;
+      }
+      const float m_use = m_run == -INFINITY ? 0.f : m_run;
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 64; ++c) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e0 = fast_exp2(s[c * 64 + 2 * i] - m_use);
+          const float e1 = fast_exp2(s[c * 64 + 2 * i + 1] - m_use);
+          sum += e0 + e1;
+          pk[i] = pack_half2(e0, e1);
+        }
+        tc::tmem_st32(sb + c * 32, pk);
+      }
+      l_run = l_run * corr + sum;
+      if (grow && k > 0) {
+        // S_X(t) landed, so PV_X(t-1) has too: rescale O_X
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          float o[32];
+          tc::tmem_ld32(ob + c * 32, o);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] *= corr;
+          tc::tmem_st32(ob + c * 32, reinterpret_cast<const uint32_t*>(o));
+        }
+      }
+      tc::tmem_wait_st();
+      tc::fence_before_sync();
+      mbar_arrive(&sy.p_ready[X]);
+    }
+    if (x1[X] > x0[X] && wait2(&sy.o_final, 0, sy, p, 42)) {
+      tc::fence_after_sync();
+      const int row = qt * 2 * BM + X * BM + r;
+      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
+      const long obase = ((long)row * p.nq + h) * HD;
+      const float* g = p.gate[seq];
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        float o[32];
+        tc::tmem_ld32(ob + c * 32, o);
+        tc::tmem_wait_ld();
+        if (row < P) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            o[i] *= inv;
+            if (g) o[i] *= 1.f / (1.f + expf(-g[obase + c * 32 + i]));
+          }
+          if (p.out_f32) {
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out[seq]) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          } else {
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out[seq]) + obase + c * 32);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_uint4(pack_half2(o[8 * i], o[8 * i + 1]), pack_half2(o[8 * i + 2], o[8 * i + 3]),
+                                  pack_half2(o[8 * i + 4], o[8 * i + 5]), pack_half2(o[8 * i + 6], o[8 * i + 7]));
+          }
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
 // ---- host side ---------------------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -413,6 +719,24 @@ int launch_prefill(PrefillParams& p, int nseq, cudaStream_t st) {
   return 0;
 }
 
+template <int HD>
+int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
+  using Geo = PGeo2<HD>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(prefill2_kernel<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
+    if (e != cudaSuccess) return record_status((int)e);
+    configured[dev] = true;
+  }
+  dim3 grid(p.ntq, p.nq, nseq);
+  prefill2_kernel<HD><<<grid, kThreads2, Geo::SMEM, st>>>(p);
+  ASPIDA_CHECK_LAUNCH();
+  return 0;
+}
+
 }  // namespace
 
 int prefill_batch(int nseq, const void* const* q, const void* const* K, const void* const* V,
@@ -450,12 +774,16 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     p.status = device_status_ptr();
     p.nq = nq; p.nkv = nkv; p.G = nq / nkv;
     p.window = window; p.out_f32 = out_f32;
-    p.ntq = (maxP + BM - 1) / BM;
     p.scale_log2 = scale * kLog2e;
     p.softcap = softcap;
-    int rc = hd == 64 ? launch_prefill<64>(p, cnt, st)
-           : hd == 128 ? launch_prefill<128>(p, cnt, st)
-                       : launch_prefill<256>(p, cnt, st);
+    int rc;
+    if (hd <= 128) {
+      p.ntq = (maxP + 2 * BM - 1) / (2 * BM);          // 256-row tiles
+      rc = hd == 64 ? launch_prefill2<64>(p, cnt, st) : launch_prefill2<128>(p, cnt, st);
+    } else {
+      p.ntq = (maxP + BM - 1) / BM;
+      rc = launch_prefill<256>(p, cnt, st);
+    }
     if (rc) return rc;
   }
   return 0;
