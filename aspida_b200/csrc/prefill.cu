@@ -115,6 +115,28 @@ __device__ __forceinline__ void scores_log2(float* x, bool capped, float cap, fl
   }
 }
 
+// Packed f32x2 arithmetic (sm_100): two lanes of fp32 per instruction.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1,%2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0,%1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // -inf outside keys max(0, qpos-window+1)..qpos and beyond the length.
 __device__ __forceinline__ void mask_chunk(float* x, int key0, int qpos, int win_lo, int len) {
   const int hi = min(qpos, len - 1);
@@ -548,6 +570,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
         for (int X = 0; X < 2; ++X) {
           if (act(X, j)) {
             if (!(ok = wait2(&sy.p_ready[X], np[X] & 1, sy, p, 32))) break;
+            TRACE(8 + X, j);
             tc::fence_after_sync();
             issue_PV(X, j, np[X] == 0);
             ++np[X];
@@ -577,6 +600,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
     int k = 0;
     for (int t = x0[X]; t < x1[X]; ++t, ++k) {
       if (!wait2(&sy.s_full[X], k & 1, sy, p, 40)) break;
+      if (r == 0) TRACE(10 + 2 * X, k);
       tc::fence_after_sync();
       const int key0 = t * BN;
       const bool masked = !(key0 + BN - 1 <= qpos && key0 >= win_lo && key0 + BN <= len);
@@ -584,14 +608,21 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) tc::tmem_ld32(sb + c * 32, s + c * 32);
       tc::tmem_wait_ld();
+      // row max: on raw scores when uncapped (scale > 0 keeps the order), so
+      // the scale folds into the exponent's FFMA below
+      if (capped) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) scores_log2(s + c * 32, true, p.softcap, p.scale_log2);
+      }
+      if (masked) {
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) mask_chunk(s + c * 32, key0 + c * 32, qpos, win_lo, len);
+      }
+      const float sc = capped ? 1.f : p.scale_log2;   // s -> log2 domain
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        scores_log2(s + c * 32, capped, p.softcap, p.scale_log2);
-        if (masked) mask_chunk(s + c * 32, key0 + c * 32, qpos, win_lo, len);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mx = fmaxf(mx, s[c * 32 + i]);
-      }
+      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
+      mx *= sc;
       // keep the stale max unless some row of this warp grew by > 2^8
       const bool grow = __any_sync(0xffffffffu, mx > m_run + kRescaleThreshold);
       float corr = 1.f;
@@ -601,19 +632,22 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
         m_run = m_new;
       }
       const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      float sum = 0.f;
+      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(-m_use, -m_use);
+      uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
       for (int c = 0; c < BN / 64; ++c) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float e0 = fast_exp2(s[c * 64 + 2 * i] - m_use);
-          const float e1 = fast_exp2(s[c * 64 + 2 * i + 1] - m_use);
-          sum += e0 + e1;
+          const float2 a = f2_unpack(f2_fma(f2_pack(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]), sc2, nm2));
+          const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
+          sum2 = f2_add(sum2, f2_pack(e0, e1));
           pk[i] = pack_half2(e0, e1);
         }
         tc::tmem_st32(sb + c * 32, pk);
       }
+      const float2 sp = f2_unpack(sum2);
+      const float sum = sp.x + sp.y;
       l_run = l_run * corr + sum;
       if (grow && k > 0) {
         // S_X(t) landed, so PV_X(t-1) has too: rescale O_X
@@ -630,6 +664,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
       tc::tmem_wait_st();
       tc::fence_before_sync();
       mbar_arrive(&sy.p_ready[X]);
+      if (r == 0) TRACE(11 + 2 * X, k);
     }
     if (x1[X] > x0[X] && wait2(&sy.o_final, 0, sy, p, 42)) {
       tc::fence_after_sync();
