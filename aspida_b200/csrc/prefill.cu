@@ -137,6 +137,48 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
+// 2^x for a pair on the FMA/ALU pipes, to offload the MUFU unit (two softmax
+// warps per SM sub-partition would otherwise saturate it). x = n + f with n
+// = round(x) taken from the bits of x + 1.5*2^23, f in [-0.5, 0.5]; 2^f by a
+// cubic fitted here by least squares on the relative error (max 7.7e-5,
+// below fp16's half-ulp, so the fp16 P is unchanged); 2^n is added to the
+// exponent bits. x is clamped at -125 (the result then rounds to 0 in fp16).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kMagic = 12582912.f;                 // 1.5 * 2^23
+  const uint64_t a = f2_pack(fmaxf(x.x, -125.f), fmaxf(x.y, -125.f));
+  const uint64_t t = f2_add(a, f2_pack(kMagic, kMagic));          // n in the low bits
+  const uint64_t f = f2_add(a, f2_add(t, f2_pack(-kMagic, -kMagic)) ^ 0x8000000080000000ull);
+  uint64_t q = f2_fma(f2_pack(0.05508872f, 0.05508872f), f, f2_pack(0.24260436f, 0.24260436f));
+  q = f2_fma(q, f, f2_pack(0.69327629f, 0.69327629f));
+  q = f2_fma(q, f, f2_pack(0.99992895f, 0.99992895f));
+  const float2 r = f2_unpack(q), tn = f2_unpack(t);
+  return make_float2(__int_as_float(__float_as_int(r.x) + (__float_as_int(tn.x) << 23)),
+                     __int_as_float(__float_as_int(r.y) + (__float_as_int(tn.y) << 23)));
+}
+
+// max(a, b, c) in one instruction (sm_100 three-input max).
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Max of 128 values as a shallow tree of three-input maxes (independent
+// partial maxima instead of one 128-long dependent chain).
+__device__ __forceinline__ float rowmax128(const float* s) {
+  float m[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = max3(s[k], s[8 + k], s[16 + k]);
+#pragma unroll
+  for (int i = 24; i + 16 <= 128; i += 16) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) m[k] = max3(m[k], s[i + k], s[i + 8 + k]);
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) m[k] = fmaxf(m[k], s[120 + k]);
+  return fmaxf(max3(m[0], m[1], m[2]), max3(max3(m[3], m[4], m[5]), m[6], m[7]));
+}
+
 // -inf outside keys max(0, qpos-window+1)..qpos and beyond the length.
 __device__ __forceinline__ void mask_chunk(float* x, int key0, int qpos, int win_lo, int len) {
   const int hi = min(qpos, len - 1);
@@ -389,18 +431,24 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
 
 
 // ---------------------------------------------------------------------------
-// Two query tiles per CTA (hd <= 128): rows A = [256*qt, +128) and
-// B = [256*qt + 128, +128) of one head share every K/V tile. Two softmax
-// warpgroups (warps 2-5 for A, 6-9 for B) ping-pong against the MMA issuer:
-// while one warpgroup turns S into P, the tensor core runs the other tile's
-// PV and next S. TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B
-// [384,512). MMAs from one thread complete in issue order, so the commit
-// that signals S_X(j) also certifies PV_X(j-1): the softmax may rescale O_X
-// right after S_X(j) lands. O is only rescaled when some row's max grew by
-// more than 2^8 (log2 domain 8): otherwise the stale max is kept, P <= 2^8
-// fits fp16, and the final 1/l uses the same max.
+// Persistent two-query-tile kernel (hd <= 128). A work item is (sequence,
+// head, 256-row tile); items are ordered heaviest first and dealt to one CTA
+// per SM round-robin. Within an item, query tiles A = rows [256*qt, +128) and
+// B = [256*qt + 128, +128) share every K/V tile; two softmax warpgroups
+// (warps 2-5 for A, 6-9 for B) ping-pong against the MMA issuer, so one
+// tile's softmax overlaps the other tile's PV and next S.
+// TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).
+// Across items: the Q buffer is released (q_empty) as soon as the item's last
+// S MMA completes, so the producer loads the next item's Q and K/V and the
+// MMA issues its first S while the softmax warpgroups are still in the
+// previous epilogue; O_X is handed back through o_full / o_free.
+// MMAs from one thread complete in issue order, so the commit that signals
+// S_X(j) also certifies PV_X(j-1): the softmax may rescale O_X right after
+// S_X(j) lands. O is only rescaled when some row's max grew by more than
+// 2^8 (log2 domain 8): otherwise the stale max is kept, P <= 2^8 fits fp16,
+// and the final 1/l uses the same max.
 // ---------------------------------------------------------------------------
-constexpr int kThreads2 = 320;
+constexpr int kThreads2 = 576;   // producer, MMA, 2 x 8 softmax warps
 constexpr float kRescaleThreshold = 8.f;
 
 template <int HD>
@@ -415,10 +463,12 @@ struct PGeo2 {
 };
 
 struct Sync2 {
-  uint64_t q_full;
+  uint64_t q_full, q_empty;
   uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
   uint64_t s_full[2], p_ready[2];   // per query tile
-  uint64_t o_final;
+  uint64_t o_full[2], o_free[2];    // per query tile
+  float xmax[2][2][2][128];         // [tile parity][query tile][column half][row]
+  float xsum[2][2][128];            // [query tile][column half][row] for the epilogue
   uint32_t tmem_base;
   int abort;
 };
@@ -435,34 +485,52 @@ __device__ __forceinline__ bool wait2(uint64_t* bar, uint32_t parity, Sync2& sy,
   return false;
 }
 
+// Geometry of one work item; identical in every role.
+struct Item {
+  int seq, h, qt, P, len, kvh;
+  int qf[2], x0[2], x1[2];   // first position, active KV tiles [x0, x1) per query tile
+  int t0, n;                 // union of KV tiles
+  bool valid;
+};
+
+template <int BN>
+__device__ __forceinline__ Item make_item(const PrefillParams& p, int nseq, int w) {
+  Item it;
+  const int per = nseq * p.nq;
+  it.qt = p.ntq - 1 - w / per;
+  const int rem = w % per;
+  it.seq = rem / p.nq;
+  it.h = rem % p.nq;
+  it.P = p.P[it.seq];
+  const int ps = p.pos_start[it.seq];
+  it.len = ps + it.P;
+  it.kvh = it.h / p.G;
+  it.valid = it.qt * 2 * BM < it.P;
+  for (int X = 0; X < 2; ++X) {
+    const int r0 = it.qt * 2 * BM + X * BM;
+    it.qf[X] = ps + r0;
+    if (r0 >= it.P) { it.x0[X] = it.x1[X] = 0; continue; }
+    const int ql = min(ps + it.P, it.qf[X] + BM) - 1;
+    const int lo = p.window > 0 ? max(0, it.qf[X] - p.window + 1) : 0;
+    it.x0[X] = lo / BN;
+    it.x1[X] = ql / BN + 1;
+  }
+  it.t0 = it.x0[0];
+  it.n = max(it.x1[0], it.x1[1]) - it.t0;
+  return it;
+}
+
+__device__ __forceinline__ bool item_act(const Item& it, int X, int j) {
+  return it.t0 + j >= it.x0[X] && it.t0 + j < it.x1[X];
+}
+
 template <int HD>
 __global__ void __launch_bounds__(kThreads2, 1)
-prefill2_kernel(const __grid_constant__ PrefillParams p) {
+prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
   using Geo = PGeo2<HD>;
   constexpr int BN = Geo::BN, CH = Geo::CH, NS = Geo::NS;
   extern __shared__ unsigned char smem_raw[];
   __shared__ Sync2 sy;
-
-  const int seq = blockIdx.z, h = blockIdx.y;
-  const int qt = p.ntq - 1 - (int)blockIdx.x;        // 256-row tile, heaviest first
-  const int P = p.P[seq], ps = p.pos_start[seq];
-  if (qt * 2 * BM >= P) return;
-  const int kvh = h / p.G;
-  const int len = ps + P;
-  // per query tile X: first/last position and active KV tile range [x0, x1)
-  int qf[2], x0[2], x1[2];
-  for (int X = 0; X < 2; ++X) {
-    const int r0 = qt * 2 * BM + X * BM;
-    qf[X] = ps + r0;
-    if (r0 >= P) { x0[X] = x1[X] = 0; continue; }
-    const int ql = min(ps + P, qf[X] + BM) - 1;
-    const int lo = p.window > 0 ? max(0, qf[X] - p.window + 1) : 0;
-    x0[X] = lo / BN;
-    x1[X] = ql / BN + 1;
-  }
-  const int t0 = x0[0];
-  const int n = max(x1[0], x1[1]) - t0;               // union of KV tiles
-  auto act = [&](int X, int j) { return t0 + j >= x0[X] && t0 + j < x1[X]; };
 
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -473,15 +541,17 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     mbar_init(&sy.q_full, 1);
+    mbar_init(&sy.q_empty, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sy.k_full[s], 1);
       mbar_init(&sy.v_full[s], 1);
       mbar_init(&sy.k_empty[s], 1);
       mbar_init(&sy.v_empty[s], 1);
       mbar_init(&sy.s_full[s], 1);
-      mbar_init(&sy.p_ready[s], 128);
+      mbar_init(&sy.p_ready[s], 256);
+      mbar_init(&sy.o_full[s], 1);
+      mbar_init(&sy.o_free[s], 256);
     }
-    mbar_init(&sy.o_final, 1);
     sy.abort = 0;
   }
   if (warp == 1) {
@@ -497,24 +567,32 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (tc::elect_one()) {
-      const int nqt = x1[1] > x0[1] ? 2 : 1;           // tile B may lie past P
-      mbar_arrive_expect_tx(&sy.q_full, nqt * Geo::QT_BYTES);
-      for (int X = 0; X < nqt; ++X)
-        for (int c = 0; c < CH; ++c)
-          tc::tma_load_2d(Qs + X * Geo::QT_BYTES + c * BM * 128, &p.qmap[seq], h * HD + c * 64,
-                          qt * 2 * BM + X * BM, &sy.q_full);
-      for (int j = 0; j < n; ++j) {
-        const int s = j % NS, row = (t0 + j) * BN;
-        if (j >= NS && !wait2(&sy.k_empty[s], ((j / NS) - 1) & 1, sy, p, 20)) break;
-        mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
-        for (int c = 0; c < CH; ++c)
-          tc::tma_load_2d(Ks + s * Geo::KV_BYTES + c * BN * 128, &p.kmap[seq], kvh * HD + c * 64,
-                          row, &sy.k_full[s]);
-        if (j >= NS && !wait2(&sy.v_empty[s], ((j / NS) - 1) & 1, sy, p, 21)) break;
-        mbar_arrive_expect_tx(&sy.v_full[s], Geo::KV_BYTES);
-        for (int c = 0; c < CH; ++c)
-          tc::tma_load_2d(Vs + s * Geo::KV_BYTES + c * BN * 128, &p.vmap[seq], kvh * HD + c * 64,
-                          row, &sy.v_full[s]);
+      long g = 0;        // K/V tiles loaded so far (stage g % NS)
+      int ic = 0;        // items started
+      for (int w = blockIdx.x; w < nitems && !sy.abort; w += gridDim.x) {
+        const Item it = make_item<BN>(p, nseq, w);
+        if (!it.valid) continue;
+        if (ic > 0 && !wait2(&sy.q_empty, (ic - 1) & 1, sy, p, 22)) break;
+        const int nqt = it.x1[1] > it.x0[1] ? 2 : 1;   // tile B may lie past P
+        mbar_arrive_expect_tx(&sy.q_full, nqt * Geo::QT_BYTES);
+        for (int X = 0; X < nqt; ++X)
+          for (int c = 0; c < CH; ++c)
+            tc::tma_load_2d(Qs + X * Geo::QT_BYTES + c * BM * 128, &p.qmap[it.seq],
+                            it.h * HD + c * 64, it.qt * 2 * BM + X * BM, &sy.q_full);
+        ++ic;
+        for (int j = 0; j < it.n; ++j, ++g) {
+          const int s = (int)(g % NS), row = (it.t0 + j) * BN;
+          if (g >= NS && !wait2(&sy.k_empty[s], ((g / NS) - 1) & 1, sy, p, 20)) break;
+          mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
+          for (int c = 0; c < CH; ++c)
+            tc::tma_load_2d(Ks + s * Geo::KV_BYTES + c * BN * 128, &p.kmap[it.seq],
+                            it.kvh * HD + c * 64, row, &sy.k_full[s]);
+          if (g >= NS && !wait2(&sy.v_empty[s], ((g / NS) - 1) & 1, sy, p, 21)) break;
+          mbar_arrive_expect_tx(&sy.v_full[s], Geo::KV_BYTES);
+          for (int c = 0; c < CH; ++c)
+            tc::tma_load_2d(Vs + s * Geo::KV_BYTES + c * BN * 128, &p.vmap[it.seq],
+                            it.kvh * HD + c * 64, row, &sy.v_full[s]);
+        }
       }
     }
     __syncwarp();
@@ -524,9 +602,11 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
       constexpr uint32_t idS = tc::idesc_f16_f32(BM, BN, false, false);
       constexpr uint32_t idO = tc::idesc_f16_f32(BM, HD, false, true);
       const uint32_t qbase = smem_u32(Qs), kbase = smem_u32(Ks), vbase = smem_u32(Vs);
-      int np[2] = {0, 0};                              // P tiles consumed per query tile
-      auto issue_S = [&](int X, int j) {
-        const int s = j % NS;
+      long g = 0;                    // K/V tiles consumed (stage g % NS)
+      int ic = 0;                    // items started
+      int np[2] = {0, 0};            // P tiles consumed per query tile (all items)
+      int no[2] = {0, 0};            // O accumulators handed to the epilogue
+      auto issue_S = [&](int X, int s) {
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
           const int c = kk >> 2;
@@ -538,8 +618,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
         }
         tc::commit(&sy.s_full[X]);
       };
-      auto issue_PV = [&](int X, int j, bool first) {
-        const int s = j % NS;
+      auto issue_PV = [&](int X, int s, bool first) {
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t b = tc::smem_desc_sw128(vbase + s * Geo::KV_BYTES + kk * 16 * 128,
@@ -548,147 +627,193 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
                      (!first || kk > 0) ? 1u : 0u);
         }
       };
-      bool ok = wait2(&sy.q_full, 0, sy, p, 30);
-      tc::fence_after_sync();
-      if (ok && n > 0) {
-        ok = wait2(&sy.k_full[0], 0, sy, p, 31);
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+        const Item it = make_item<BN>(p, nseq, w);
+        if (!it.valid) continue;
+        if (!(ok = wait2(&sy.q_full, ic & 1, sy, p, 30))) break;
+        ++ic;
         tc::fence_after_sync();
-        if (ok) {
-          if (act(0, 0)) issue_S(0, 0);
-          if (act(1, 0)) issue_S(1, 0);
-          tc::commit(&sy.k_empty[0]);
+        // first S of the item
+        {
+          const int s = (int)(g % NS);
+          if (!(ok = wait2(&sy.k_full[s], (g / NS) & 1, sy, p, 31))) break;
+          tc::fence_after_sync();
+          for (int X = 0; X < 2; ++X)
+            if (item_act(it, X, 0)) issue_S(X, s);
+          tc::commit(&sy.k_empty[s]);
+          if (it.n == 1) tc::commit(&sy.q_empty);
         }
-      }
-      for (int j = 0; ok && j < n; ++j) {
-        const int s = j % NS;
-        if (!(ok = wait2(&sy.v_full[s], (j / NS) & 1, sy, p, 33))) break;
-        const bool more = j + 1 < n;
-        if (more) {
-          if (!(ok = wait2(&sy.k_full[(j + 1) % NS], ((j + 1) / NS) & 1, sy, p, 31))) break;
-        }
-        tc::fence_after_sync();
-        for (int X = 0; X < 2; ++X) {
-          if (act(X, j)) {
-            if (!(ok = wait2(&sy.p_ready[X], np[X] & 1, sy, p, 32))) break;
-            TRACE(8 + X, j);
-            tc::fence_after_sync();
-            issue_PV(X, j, np[X] == 0);
-            ++np[X];
+        for (int j = 0; ok && j < it.n; ++j) {
+          const int s = (int)((g + j) % NS);
+          if (!(ok = wait2(&sy.v_full[s], ((g + j) / NS) & 1, sy, p, 33))) break;
+          const bool more = j + 1 < it.n;
+          const int s1 = (int)((g + j + 1) % NS);
+          if (more && !(ok = wait2(&sy.k_full[s1], ((g + j + 1) / NS) & 1, sy, p, 31))) break;
+          tc::fence_after_sync();
+          for (int X = 0; X < 2; ++X) {
+            if (item_act(it, X, j)) {
+              const bool first = it.t0 + j == it.x0[X];
+              if (first && no[X] > 0 && !(ok = wait2(&sy.o_free[X], (no[X] - 1) & 1, sy, p, 34)))
+                break;
+              if (!(ok = wait2(&sy.p_ready[X], np[X] & 1, sy, p, 32))) break;
+              TRACE(10 + X, np[X]);
+              tc::fence_after_sync();
+              issue_PV(X, s, first);
+              ++np[X];
+              if (it.t0 + j + 1 == it.x1[X]) {      // last PV of X in this item
+                tc::commit(&sy.o_full[X]);
+                ++no[X];
+              }
+            }
+            if (more && item_act(it, X, j + 1)) issue_S(X, s1);
           }
-          if (more && act(X, j + 1)) issue_S(X, j + 1);
+          if (!ok) break;
+          if (more) {
+            tc::commit(&sy.k_empty[s1]);
+            if (j + 2 == it.n) tc::commit(&sy.q_empty);   // last S of the item issued
+          }
+          tc::commit(&sy.v_empty[s]);
         }
-        if (!ok) break;
-        if (more) tc::commit(&sy.k_empty[(j + 1) % NS]);
-        tc::commit(&sy.v_empty[s]);
+        g += it.n;
       }
-      tc::commit(&sy.o_final);
+      // drain: every issued MMA completes before TMEM is released
+      tc::commit(&sy.q_empty);
+      mbar_wait_bounded(&sy.q_empty, ic & 1);
     }
     __syncwarp();
   } else {
     // ------------------------------ softmax / epilogue ------------------------
-    const int X = warp < 6 ? 0 : 1;                   // query tile of this warpgroup
+    // Warps 2-9 serve query tile A, 10-17 tile B. Each row is split between
+    // two threads (column halves) in warps with the same TMEM lane quarter;
+    // they exchange partial row maxima through shared memory behind a
+    // 64-thread named barrier, which also orders the P writes after both
+    // halves have read their S columns.
+    const int sw = warp - 2;
+    const int X = sw >> 3;                            // query tile of this warp
+    const int half = (sw >> 2) & 1;                   // column half of S / O
     const int lane = threadIdx.x & 31;
     const int wq = warp & 3;
     const int r = wq * 32 + lane;                     // row in tile == TMEM lane
+    const int bar_id = 1 + X * 4 + wq;                // pairs the two halves
+    constexpr int HB = BN / 2;                        // S columns per thread
+    constexpr int HO = HD / 2;                        // O columns per thread
     const uint32_t lane_addr = (uint32_t)(wq * 32) << 16;
     const uint32_t sb = tmem + lane_addr + X * 128;
-    const uint32_t ob = tmem + lane_addr + 256 + X * 128;
-    const int qpos = qf[X] + r;
-    const int win_lo = p.window > 0 ? qpos - p.window + 1 : 0;
+    const uint32_t ob = tmem + lane_addr + 256 + X * 128 + half * HO;
     const bool capped = p.softcap > 0.f;
-    float m_run = -INFINITY, l_run = 0.f;
-    int k = 0;
-    for (int t = x0[X]; t < x1[X]; ++t, ++k) {
-      if (!wait2(&sy.s_full[X], k & 1, sy, p, 40)) break;
-      if (r == 0) TRACE(10 + 2 * X, k);
-      tc::fence_after_sync();
-      const int key0 = t * BN;
-      const bool masked = !(key0 + BN - 1 <= qpos && key0 >= win_lo && key0 + BN <= len);
-      float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tc::tmem_ld32(sb + c * 32, s + c * 32);
-      tc::tmem_wait_ld();
-      // row max: on raw scores when uncapped (scale > 0 keeps the order), so
-      // the scale folds into the exponent's FFMA below
-      if (capped) {
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) scores_log2(s + c * 32, true, p.softcap, p.scale_log2);
-      }
-      if (masked) {
-#pragma unroll
-        for (int c = 0; c < BN / 32; ++c) mask_chunk(s + c * 32, key0 + c * 32, qpos, win_lo, len);
-      }
-      const float sc = capped ? 1.f : p.scale_log2;   // s -> log2 domain
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BN; ++i) mx = fmaxf(mx, s[i]);
-      mx *= sc;
-      // keep the stale max unless some row of this warp grew by > 2^8
-      const bool grow = __any_sync(0xffffffffu, mx > m_run + kRescaleThreshold);
-      float corr = 1.f;
-      if (grow) {
-        const float m_new = fmaxf(m_run, mx);
-        corr = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
-        m_run = m_new;
-      }
-      const float m_use = m_run == -INFINITY ? 0.f : m_run;
-      const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(-m_use, -m_use);
-      uint64_t sum2 = f2_pack(0.f, 0.f);
-#pragma unroll
-      for (int c = 0; c < BN / 64; ++c) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float2 a = f2_unpack(f2_fma(f2_pack(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]), sc2, nm2));
-          const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
-          sum2 = f2_add(sum2, f2_pack(e0, e1));
-          pk[i] = pack_half2(e0, e1);
+    const float sc = capped ? 1.f : p.scale_log2;     // s -> log2 domain
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
+    int ks = 0;                                       // S tiles consumed (all items)
+    int ne = 0;                                       // epilogues done
+    for (int w = blockIdx.x; w < nitems && !sy.abort; w += gridDim.x) {
+      const Item it = make_item<BN>(p, nseq, w);
+      if (!it.valid || it.x1[X] <= it.x0[X]) continue;
+      const int qpos = it.qf[X] + r;
+      const int win_lo = p.window > 0 ? qpos - p.window + 1 : 0;
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      for (int t = it.x0[X]; t < it.x1[X]; ++t, ++ks) {
+        if (!(ok = wait2(&sy.s_full[X], ks & 1, sy, p, 40))) break;
+        tc::fence_after_sync();
+        const int key0 = t * BN + half * HB;
+        const bool masked = !(key0 + HB - 1 <= qpos && key0 >= win_lo && key0 + HB <= it.len);
+        float s[HB];
+        tc::tmem_ld32(sb + half * HB, s);
+        tc::tmem_ld32(sb + half * HB + 32, s + 32);
+        tc::tmem_wait_ld();
+        if (capped) {
+          scores_log2(s, true, p.softcap, p.scale_log2);
+          scores_log2(s + 32, true, p.softcap, p.scale_log2);
         }
-        tc::tmem_st32(sb + c * 32, pk);
-      }
-      const float2 sp = f2_unpack(sum2);
-      const float sum = sp.x + sp.y;
-      l_run = l_run * corr + sum;
-      if (grow && k > 0) {
-        // S_X(t) landed, so PV_X(t-1) has too: rescale O_X
-#pragma unroll 1
-        for (int c = 0; c < HD / 32; ++c) {
-          float o[32];
-          tc::tmem_ld32(ob + c * 32, o);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] *= corr;
-          tc::tmem_st32(ob + c * 32, reinterpret_cast<const uint32_t*>(o));
+        if (masked) {
+          mask_chunk(s, key0, qpos, win_lo, it.len);
+          mask_chunk(s + 32, key0 + 32, qpos, win_lo, it.len);
         }
-      }
-      tc::tmem_wait_st();
-      tc::fence_before_sync();
-      mbar_arrive(&sy.p_ready[X]);
-      if (r == 0) TRACE(11 + 2 * X, k);
-    }
-    if (x1[X] > x0[X] && wait2(&sy.o_final, 0, sy, p, 42)) {
-      tc::fence_after_sync();
-      const int row = qt * 2 * BM + X * BM + r;
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      const long obase = ((long)row * p.nq + h) * HD;
-      const float* g = p.gate[seq];
+        // partial max (raw scores when uncapped: scale > 0 keeps the order)
+        float m8[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = max3(s[k], s[8 + k], s[16 + k]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = max3(m8[k], s[24 + k], s[32 + k]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = max3(m8[k], s[40 + k], s[48 + k]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) m8[k] = fmaxf(m8[k], s[56 + k]);
+        float mx = fmaxf(max3(m8[0], m8[1], m8[2]), max3(max3(m8[3], m8[4], m8[5]), m8[6], m8[7]));
+        sy.xmax[ks & 1][X][half][r] = mx;
+        pair_sync();                                  // both halves have read S
+        mx = fmaxf(mx, sy.xmax[ks & 1][X][half ^ 1][r]) * sc;
+        // keep the stale max unless some row of this warp grew by > 2^8
+        const bool grow = __any_sync(0xffffffffu, mx > m_run + kRescaleThreshold);
+        float corr = 1.f;
+        if (grow) {
+          const float m_new = fmaxf(m_run, mx);
+          corr = m_new == -INFINITY ? 1.f : fast_exp2(m_run - m_new);
+          m_run = m_new;
+        }
+        const float m_use = m_run == -INFINITY ? 0.f : m_run;
+        const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(-m_use, -m_use);
+        uint64_t sum2[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sum2[u] = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 a = f2_unpack(f2_fma(f2_pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sc2, nm2));
+            const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
+            sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(e0, e1));
+            pk[i] = pack_half2(e0, e1);
+          }
+          tc::tmem_st16(sb + half * (HB / 2) + c * 16, pk);
+        }
+        const float2 sp = f2_unpack(f2_add(f2_add(sum2[0], sum2[1]), f2_add(sum2[2], sum2[3])));
+        l_run = l_run * corr + (sp.x + sp.y);
+        if (grow && t > it.x0[X]) {
+          // S_X(t) landed, so PV_X(t-1) has too: rescale this half of O_X
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
+          for (int c = 0; c < HO / 32; ++c) {
+            float o[32];
+            tc::tmem_ld32(ob + c * 32, o);
+            tc::tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= corr;
+            tc::tmem_st32(ob + c * 32, reinterpret_cast<const uint32_t*>(o));
+          }
+        }
+        tc::tmem_wait_st();
+        tc::fence_before_sync();
+        mbar_arrive(&sy.p_ready[X]);
+      }
+      if (!ok || !wait2(&sy.o_full[X], ne & 1, sy, p, 42)) break;
+      tc::fence_after_sync();
+      sy.xsum[X][half][r] = l_run;
+      pair_sync();
+      const float l_tot = l_run + sy.xsum[X][half ^ 1][r];
+      pair_sync();                                    // xsum reusable by the next item
+      const int row = it.qt * 2 * BM + X * BM + r;
+      const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      const long obase = ((long)row * p.nq + it.h) * HD + half * HO;
+      const float* gt = p.gate[it.seq];
+#pragma unroll 1
+      for (int c = 0; c < HO / 32; ++c) {
         float o[32];
         tc::tmem_ld32(ob + c * 32, o);
         tc::tmem_wait_ld();
-        if (row < P) {
+        if (row < it.P) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) {
             o[i] *= inv;
-            if (g) o[i] *= 1.f / (1.f + expf(-g[obase + c * 32 + i]));
+            if (gt) o[i] *= 1.f / (1.f + expf(-gt[obase + c * 32 + i]));
           }
           if (p.out_f32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out[seq]) + obase + c * 32);
+            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out[it.seq]) + obase + c * 32);
 #pragma unroll
             for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
           } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out[seq]) + obase + c * 32);
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out[it.seq]) + obase + c * 32);
 #pragma unroll
             for (int i = 0; i < 4; ++i)
               dst[i] = make_uint4(pack_half2(o[8 * i], o[8 * i + 1]), pack_half2(o[8 * i + 2], o[8 * i + 3]),
@@ -696,6 +821,9 @@ prefill2_kernel(const __grid_constant__ PrefillParams p) {
           }
         }
       }
+      tc::fence_before_sync();
+      mbar_arrive(&sy.o_free[X]);                      // O_X may be overwritten
+      ++ne;
     }
   }
   tc::fence_before_sync();
@@ -766,8 +894,9 @@ int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
     if (e != cudaSuccess) return record_status((int)e);
     configured[dev] = true;
   }
-  dim3 grid(p.ntq, p.nq, nseq);
-  prefill2_kernel<HD><<<grid, kThreads2, Geo::SMEM, st>>>(p);
+  const int nitems = p.ntq * p.nq * nseq;
+  const int grid = std::min(nitems, num_sms());
+  prefill2_kernel<HD><<<grid, kThreads2, Geo::SMEM, st>>>(p, nseq, nitems);
   ASPIDA_CHECK_LAUNCH();
   return 0;
 }
