@@ -57,6 +57,7 @@ struct PrefillParams {
   CUtensorMap qmap[kMaxSeq];
   CUtensorMap kmap[kMaxSeq];
   CUtensorMap vmap[kMaxSeq];
+  CUtensorMap omap[kMaxSeq];        // fp16 output (TMA-store epilogue); unused for f32 out
   void* out[kMaxSeq];
   const float* gate[kMaxSeq];
   int P[kMaxSeq];
@@ -438,10 +439,10 @@ prefill_kernel(const __grid_constant__ PrefillParams p) {
 // (warps 2-5 for A, 6-9 for B) ping-pong against the MMA issuer, so one
 // tile's softmax overlaps the other tile's PV and next S.
 // TMEM: S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).
-// Across items: the Q buffer is released (q_empty) as soon as the item's last
-// S MMA completes, so the producer loads the next item's Q and K/V and the
-// MMA issues its first S while the softmax warpgroups are still in the
-// previous epilogue; O_X is handed back through o_full / o_free.
+// Across items: K/V keep streaming; each query tile's epilogue stages its fp16
+// output in that tile's Q buffer (idle once O is final) and writes it with a
+// TMA tensor store, then hands the buffer back (q_free) for the next item's
+// Q; O_X is handed back through o_full / o_free.
 // MMAs from one thread complete in issue order, so the commit that signals
 // S_X(j) also certifies PV_X(j-1): the softmax may rescale O_X right after
 // S_X(j) lands. O is only rescaled when some row's max grew by more than
@@ -463,10 +464,11 @@ struct PGeo2 {
 };
 
 struct Sync2 {
-  uint64_t q_full, q_empty;
+  uint64_t q_full, q_free[2];       // Q buffer of tile X released after its epilogue
   uint64_t k_full[2], v_full[2], k_empty[2], v_empty[2];
   uint64_t s_full[2], p_ready[2];   // per query tile
   uint64_t o_full[2], o_free[2];    // per query tile
+  uint64_t drain;
   float xmax[2][2][2][128];         // [tile parity][query tile][column half][row]
   float xsum[2][2][128];            // [query tile][column half][row] for the epilogue
   uint32_t tmem_base;
@@ -501,8 +503,11 @@ __device__ __forceinline__ Item make_item(const PrefillParams& p, int nseq, int 
   const int rem = w % per;
   it.seq = rem / p.nq;
   it.h = rem % p.nq;
-  it.P = p.P[it.seq];
-  const int ps = p.pos_start[it.seq];
+  int P = 0, ps = 0;
+#pragma unroll
+  for (int s = 0; s < kMaxSeq; ++s)      // compile-time indices: no local copy of the params
+    if (s == it.seq) { P = p.P[s]; ps = p.pos_start[s]; }
+  it.P = P;
   it.len = ps + it.P;
   it.kvh = it.h / p.G;
   it.valid = it.qt * 2 * BM < it.P;
@@ -541,8 +546,9 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     mbar_init(&sy.q_full, 1);
-    mbar_init(&sy.q_empty, 1);
+    mbar_init(&sy.drain, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&sy.q_free[s], 1);
       mbar_init(&sy.k_full[s], 1);
       mbar_init(&sy.v_full[s], 1);
       mbar_init(&sy.k_empty[s], 1);
@@ -563,17 +569,36 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = sy.tmem_base;
+  // items are dealt boustrophedon-wise (round rr: CTA c takes the c-th item, or
+  // the (C-1-c)-th on odd rounds) over the heaviest-first list, which evens out
+  // the per-CTA load
+  auto snake_item = [&](int rr) {
+    const int c = (rr & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
+    return rr * (int)gridDim.x + c;
+  };
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (tc::elect_one()) {
       long g = 0;        // K/V tiles loaded so far (stage g % NS)
+      int qrel[2] = {0, 0};      // q_free arrivals expected so far per query tile
+      bool pend[2] = {false, false};
       int ic = 0;        // items started
-      for (int w = blockIdx.x; w < nitems && !sy.abort; w += gridDim.x) {
+      for (int rr = 0; rr * (int)gridDim.x < nitems && !sy.abort; ++rr) {
+        const int w = snake_item(rr);
+        if (w >= nitems) continue;
         const Item it = make_item<BN>(p, nseq, w);
         if (!it.valid) continue;
-        if (ic > 0 && !wait2(&sy.q_empty, (ic - 1) & 1, sy, p, 22)) break;
+        // the previous item's epilogues must have released the Q buffer
+        bool okq = true;
+        for (int X = 0; X < 2 && okq; ++X)
+          if (pend[X]) okq = wait2(&sy.q_free[X], (qrel[X] - 1) & 1, sy, p, 22);
+        if (!okq) break;
         const int nqt = it.x1[1] > it.x0[1] ? 2 : 1;   // tile B may lie past P
+        for (int X = 0; X < 2; ++X) {
+          pend[X] = X < nqt;
+          qrel[X] += X < nqt;
+        }
         mbar_arrive_expect_tx(&sy.q_full, nqt * Geo::QT_BYTES);
         for (int X = 0; X < nqt; ++X)
           for (int c = 0; c < CH; ++c)
@@ -628,7 +653,9 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
         }
       };
       bool ok = true;
-      for (int w = blockIdx.x; ok && w < nitems; w += gridDim.x) {
+      for (int rr = 0; ok && rr * (int)gridDim.x < nitems; ++rr) {
+        const int w = snake_item(rr);
+        if (w >= nitems) continue;
         const Item it = make_item<BN>(p, nseq, w);
         if (!it.valid) continue;
         if (!(ok = wait2(&sy.q_full, ic & 1, sy, p, 30))) break;
@@ -642,7 +669,6 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
           for (int X = 0; X < 2; ++X)
             if (item_act(it, X, 0)) issue_S(X, s);
           tc::commit(&sy.k_empty[s]);
-          if (it.n == 1) tc::commit(&sy.q_empty);
         }
         for (int j = 0; ok && j < it.n; ++j) {
           const int s = (int)((g + j) % NS);
@@ -669,17 +695,14 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
             if (more && item_act(it, X, j + 1)) issue_S(X, s1);
           }
           if (!ok) break;
-          if (more) {
-            tc::commit(&sy.k_empty[s1]);
-            if (j + 2 == it.n) tc::commit(&sy.q_empty);   // last S of the item issued
-          }
+          if (more) tc::commit(&sy.k_empty[s1]);
           tc::commit(&sy.v_empty[s]);
         }
         g += it.n;
       }
       // drain: every issued MMA completes before TMEM is released
-      tc::commit(&sy.q_empty);
-      mbar_wait_bounded(&sy.q_empty, ic & 1);
+      tc::commit(&sy.drain);
+      mbar_wait_bounded(&sy.drain, 0);
     }
     __syncwarp();
   } else {
@@ -706,7 +729,9 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
     auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
     int ks = 0;                                       // S tiles consumed (all items)
     int ne = 0;                                       // epilogues done
-    for (int w = blockIdx.x; w < nitems && !sy.abort; w += gridDim.x) {
+    for (int rr = 0; rr * (int)gridDim.x < nitems && !sy.abort; ++rr) {
+        const int w = snake_item(rr);
+        if (w >= nitems) continue;
       const Item it = make_item<BN>(p, nseq, w);
       if (!it.valid || it.x1[X] <= it.x0[X]) continue;
       const int qpos = it.qf[X] + r;
@@ -793,38 +818,61 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
       pair_sync();
       const float l_tot = l_run + sy.xsum[X][half ^ 1][r];
       pair_sync();                                    // xsum reusable by the next item
-      const int row = it.qt * 2 * BM + X * BM + r;
+      const int row0 = it.qt * 2 * BM + X * BM, row = row0 + r;
       const float inv = l_tot > 0.f ? 1.f / l_tot : 0.f;
+      const float* gt = nullptr;
+      void* outp = nullptr;
+#pragma unroll
+      for (int s = 0; s < kMaxSeq; ++s)
+        if (s == it.seq) { gt = p.gate[s]; outp = p.out[s]; }
       const long obase = ((long)row * p.nq + it.h) * HD + half * HO;
-      const float* gt = p.gate[it.seq];
-#pragma unroll 1
-      for (int c = 0; c < HO / 32; ++c) {
-        float o[32];
-        tc::tmem_ld32(ob + c * 32, o);
-        tc::tmem_wait_ld();
-        if (row < it.P) {
+      float o[HO];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            o[i] *= inv;
-            if (gt) o[i] *= 1.f / (1.f + expf(-gt[obase + c * 32 + i]));
-          }
-          if (p.out_f32) {
-            float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out[it.seq]) + obase + c * 32);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
-          } else {
-            uint4* dst = reinterpret_cast<uint4*>(static_cast<__half*>(p.out[it.seq]) + obase + c * 32);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_uint4(pack_half2(o[8 * i], o[8 * i + 1]), pack_half2(o[8 * i + 2], o[8 * i + 3]),
-                                  pack_half2(o[8 * i + 4], o[8 * i + 5]), pack_half2(o[8 * i + 6], o[8 * i + 7]));
-          }
-        }
-      }
+      for (int c = 0; c < HO / 32; ++c) tc::tmem_ld32(ob + c * 32, o + c * 32);
+      tc::tmem_wait_ld();
       tc::fence_before_sync();
       mbar_arrive(&sy.o_free[X]);                      // O_X may be overwritten
+#pragma unroll
+      for (int i = 0; i < HO; ++i) o[i] *= inv;
+      if (gt && row < it.P) {
+#pragma unroll
+        for (int i = 0; i < HO; ++i) o[i] *= 1.f / (1.f + expf(-gt[obase + i]));
+      }
+      const bool leader = (sw & 7) == 0 && lane == 0;  // one thread per query tile
+      if (!p.out_f32) {
+        // stage the fp16 tile in this tile's (now idle) Q buffer, in the
+        // 128-byte-swizzled layout of the TMA box, then store it with TMA
+        // (rows past P are clipped by the tensor map)
+        unsigned char* stg = Qs + X * Geo::QT_BYTES;
+#pragma unroll
+        for (int i8 = 0; i8 < HO / 8; ++i8) {
+          const int col = half * HO + i8 * 8, chunk = col >> 6, cin = (col & 63) >> 3;
+          const uint4 v = make_uint4(pack_half2(o[8 * i8], o[8 * i8 + 1]),
+                                     pack_half2(o[8 * i8 + 2], o[8 * i8 + 3]),
+                                     pack_half2(o[8 * i8 + 4], o[8 * i8 + 5]),
+                                     pack_half2(o[8 * i8 + 6], o[8 * i8 + 7]));
+          *reinterpret_cast<uint4*>(stg + chunk * BM * 128 + r * 128 + ((cin ^ (r & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        asm volatile("bar.sync %0, 256;" ::"r"(9 + X) : "memory");
+        if (leader) {
+          for (int c = 0; c < CH; ++c)
+            tc::tma_store_2d(&p.omap[it.seq], it.h * HD + c * 64, row0, stg + c * BM * 128);
+          tc::bulk_commit_group();
+          tc::bulk_wait_read();
+          mbar_arrive(&sy.q_free[X]);                 // the producer may reload Q
+        }
+      } else {
+        if (row < it.P) {
+          float4* dst = reinterpret_cast<float4*>(static_cast<float*>(outp) + obase);
+#pragma unroll
+          for (int i = 0; i < HO / 4; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        }
+        if (leader) mbar_arrive(&sy.q_free[X]);       // Q is idle once O is final
+      }
       ++ne;
     }
+    if ((sw & 7) == 0 && (threadIdx.x & 31) == 0) tc::bulk_wait_all();  // stores landed
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -927,6 +975,8 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
       if (!make_map(&p.qmap[i], q[s], (long)nq * hd, Pv, BM) ||
           !make_map(&p.kmap[i], K[s], (long)nkv * hd, len, box_kv) ||
           !make_map(&p.vmap[i], V[s], (long)nkv * hd, len, box_kv))
+        return record_status(ASPIDA_ERR_ARG);
+      if (!out_f32 && !make_map(&p.omap[i], out[s], (long)nq * hd, Pv, BM))
         return record_status(ASPIDA_ERR_ARG);
       p.out[i] = out[s];
       p.gate[i] = gate ? gate[s] : nullptr;
