@@ -73,6 +73,14 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def peaks_tensor():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
 def traffic_from_profile():
     """dram bytes per decode call from the committed ncu summary, if any."""
     p = os.path.join(ROOT, "profiles", "decode_cfg2.md")
@@ -155,6 +163,50 @@ def cpu_baseline(lens_list, seconds, K_host, V_host, q_host):
             "kind": "port",
             "sample": f"full cfg-2 batch (B=32, {sum(lens_list)} keys), {reps} reps in {el:.1f} s, "
                       "C++ restatement of the Ada attention loops, one (seq x head) job per task"}
+
+
+def prefill_leg(ab, torch, dev, seed, steps, warmup, stream):
+    """causal prefill of 4 x 4096 tokens, 32/8 heads, hd 128,
+    fp16 Q/K/V (seeded N(0,1)), fp16 output; one launch per step. Returns
+    (ms per step, causal flops per step, host inputs for the CPU sample)."""
+    nq, nkv, hd, S, NB = 32, 8, 128, 4096, 4
+    g = torch.Generator(device=dev).manual_seed(seed)
+    qs = [torch.randn(S, nq * hd, generator=g, device=dev).half() for _ in range(NB)]
+    Ks = [torch.randn(S, nkv * hd, generator=g, device=dev).half() for _ in range(NB)]
+    Vs = [torch.randn(S, nkv * hd, generator=g, device=dev).half() for _ in range(NB)]
+    outs = [torch.empty(S, nq * hd, device=dev, dtype=torch.half) for _ in range(NB)]
+    for _ in range(max(3, warmup)):
+        ab.prefill_batch(qs, Ks, Vs, nq, nkv, hd, outs=outs, stream=stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        ab.prefill_batch(qs, Ks, Vs, nq, nkv, hd, outs=outs, stream=stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = NB * nq * 2 * hd * S * (S + 1)
+    return ms, flops, (qs[0], Ks[0], Vs[0])
+
+
+def prefill_cpu_sample(q, K, V, seconds=8.0):
+    """CPU oracle on the last rows of one config-3 sequence (causal flops of
+    those rows / time), all host cores."""
+    import oracle
+    nq, nkv, hd = 32, 8, 128
+    S = q.shape[0]
+    qh, Kh, Vh = q.float().cpu().numpy(), K.float().cpu().numpy(), V.float().cpu().numpy()
+    threads = os.cpu_count() or 1
+    rows, t0, reps = list(range(S - 16, S)), time.perf_counter(), 0
+    while True:
+        oracle.prefill(qh, Kh, Vh, 0, nq, nkv, hd, rows=rows, threads=threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 100:
+            break
+    fl = sum(nq * 4 * hd * (r + 1) for r in rows)
+    return {"value": round(fl * reps / el / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "sample": f"last 16 query rows of one 4096-token sequence, {reps} reps"}
 
 
 def host_batch(seed, lens):
@@ -302,16 +354,30 @@ def main():
     torch.cuda.synchronize()
     ms_e2e = f0.elapsed_time(f1) / args.steps
 
+    # ---- prefill leg (per rank) ----
+    for c in caches:
+        c.free()
+    caches = []
+    torch.cuda.empty_cache()
+    p_steps = max(5, min(args.steps, 50))
+    p_ms, p_flops, p_sample = prefill_leg(ab, torch, dev, 2000 + rank, p_steps, args.warmup,
+                                          stream)
+    if ab.device_status() != 0:
+        raise RuntimeError("device status after prefill")
+
     nbytes = algo_bytes(lens)
-    stats = torch.tensor([ms, ms_e2e, float(nbytes)], dtype=torch.float64, device=dev)
+    stats = torch.tensor([ms, ms_e2e, p_ms, float(nbytes), float(p_flops)], dtype=torch.float64,
+                         device=dev)
     if dist:
-        mx = stats[:2].clone()
+        mx = stats[:3].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = stats[2:].clone()
+        tot = stats[3:].clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms_max, ms_e2e_max, bytes_all = float(mx[0]), float(mx[1]), float(tot[0])
+        ms_max, ms_e2e_max, p_ms_max = float(mx[0]), float(mx[1]), float(mx[2])
+        bytes_all, flops_all = float(tot[0]), float(tot[1])
     else:
-        ms_max, ms_e2e_max, bytes_all = ms, ms_e2e, float(nbytes)
+        ms_max, ms_e2e_max, p_ms_max = ms, ms_e2e, p_ms
+        bytes_all, flops_all = float(nbytes), float(p_flops)
 
     if rank == 0:
         hbm, src = peaks()
@@ -345,14 +411,26 @@ def main():
                     "ms_per_step": round(ms_e2e_max, 5)},
             "gpu_launches": args.steps * 2,   # decode_kernel + combine_kernel per step
             "clocks": clocks,
+            "prefill": {
+                "metric": "prefill attn TFLOP/s (cfg3: causal 4 x 4096, 32/8 heads, hd128, fp16)",
+                "value": round(flops_all / (p_ms_max * 1e-3) / 1e12, 2),
+                "unit": "TFLOP/s", "ms_per_step": round(p_ms_max, 4), "steps": p_steps,
+                "flops_per_step_per_gpu": p_flops,
+                "roofline": {"bound": "tensor",
+                             "achieved": round(p_flops / (p_ms * 1e-3) / 1e12, 2),
+                             "peak": peaks_tensor()[0], "unit": "TFLOP/s",
+                             "frac": round(p_flops / (p_ms * 1e-3) / 1e12 / peaks_tensor()[0], 4),
+                             "traffic": None,
+                             "peak_source": f"{peaks_tensor()[1]} bf16_tflops (cuBLAS, burst)"},
+                "gpu_launches": p_steps,
+            },
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(lens, args.cpu_seconds,
                                                 [k.float().numpy() for k in Ks_h],
                                                 [v.float().numpy() for v in Vs_h], q_h.numpy())
+            line["prefill"]["cpu_baseline"] = prefill_cpu_sample(*p_sample)
         print(json.dumps(line), flush=True)
-    for c in caches:
-        c.free()
     if dist:
         dist.destroy_process_group()
 
