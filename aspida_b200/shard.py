@@ -1,0 +1,170 @@
+"""Multi-GPU partitioning of the attention path (one process per GPU).
+
+The reference has no multi-GPU inference (its only distributed code is a TCP
+gradient exchange for training, gpu/dp_node.cu), so these are new parts:
+
+* Batched decode and prefill shard by sequence: independent units, no
+  collective on the data path. ``plan_sequences`` balances the KV bytes
+  (sum of lengths) over ranks with a longest-first greedy assignment.
+* Single long-sequence decode splits the KV cache into contiguous chunks
+  (``kv_chunks``); each rank attends its chunk and produces the split-KV
+  partial (m, l, o) per query head (aspida_attn_decode_partial), the ranks
+  exchange the partials with one all-gather over NCCL, and every rank merges
+  them with the log-sum-exp merge of gpu/fattn_sk.cu:84-97
+  (aspida_attn_merge). The payload is nq*(hd+2) floats per sequence per rank
+  (33 KB at 64 heads x hd 128), so the exchange is latency-bound.
+
+Failures: a collective that fails (a rank died or timed out) raises
+:class:`ShardError`; no rank waits forever, the process-group timeout bounds
+every exchange.
+"""
+from __future__ import annotations
+
+import heapq
+from typing import Callable, List, Optional, Sequence, Tuple
+
+import torch
+
+
+class ShardError(RuntimeError):
+    pass
+
+
+def plan_sequences(lens: Sequence[int], world: int) -> List[List[int]]:
+    """Assign sequence indices to ranks, balancing sum(len) (longest first)."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    heap = [(0, r) for r in range(world)]
+    out: List[List[int]] = [[] for _ in range(world)]
+    for i in sorted(range(len(lens)), key=lambda i: (-lens[i], i)):
+        load, r = heapq.heappop(heap)
+        out[r].append(i)
+        heapq.heappush(heap, (load + int(lens[i]), r))
+    for r in out:
+        r.sort()
+    return out
+
+
+def kv_chunks(length: int, world: int, align: int = 16) -> List[Tuple[int, int]]:
+    """Contiguous [lo, hi) key ranges of a cache of `length` rows, one per
+    rank, as equal as possible with boundaries on `align`-row multiples."""
+    if world <= 0:
+        raise ValueError("world must be positive")
+    units = (length + align - 1) // align
+    out = []
+    for r in range(world):
+        lo = min(length, (r * units // world) * align)
+        hi = min(length, ((r + 1) * units // world) * align)
+        out.append((lo, hi))
+    return out
+
+
+def pack_partials(m: torch.Tensor, l: torch.Tensor, o: torch.Tensor) -> torch.Tensor:
+    """(m [B,nq], l [B,nq], o [B,nq,hd]) -> one flat f32 buffer for the exchange."""
+    return torch.cat([m.reshape(-1), l.reshape(-1), o.reshape(-1)])
+
+
+def unpack_partials(buf: torch.Tensor, world: int, B: int, nq: int, hd: int):
+    """Gathered [world * per] buffer -> m, l [world, B*nq]; o [world, B*nq, hd]."""
+    per = B * nq * (hd + 2)
+    g = buf.reshape(world, per)
+    m = g[:, :B * nq]
+    l = g[:, B * nq:2 * B * nq]
+    o = g[:, 2 * B * nq:].reshape(world, B * nq, hd)
+    return m.contiguous(), l.contiguous(), o.contiguous()
+
+
+def exchange_partials(m, l, o, group=None) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """All-gather every rank's partial (one collective)."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    B, nq = m.shape
+    hd = o.shape[-1]
+    mine = pack_partials(m, l, o)
+    gathered = torch.empty(world * mine.numel(), dtype=mine.dtype, device=mine.device)
+    try:
+        dist.all_gather_into_tensor(gathered, mine, group=group)
+    except Exception as e:  # a peer died, timed out or the group was torn down
+        raise ShardError(f"partial exchange failed: {e}") from e
+    return unpack_partials(gathered, world, B, nq, hd)
+
+
+class SeqParallelDecode:
+    """Sequence-parallel decode with every buffer allocated once.
+
+    Per call: the split-KV partial kernel writes this rank's (m, l, o) straight
+    into a packed send buffer [m | l | o]; one all-gather (NCCL) fills the
+    receive buffer [world][m | l | o]; the strided merge kernel reads it in
+    place. No host synchronisation and no extra device copies.
+
+    K_chunks / V_chunks: this rank's fp16 chunk [rows >= n_local, nkv*hd] of
+    each of the B sequences' caches; rows 0..n_local-1 are attended."""
+
+    def __init__(self, K_chunks, V_chunks, n_local: int, nq: int, nkv: int, hd: int, *,
+                 scale: Optional[float] = None, softcap: float = 0.0, group=None):
+        import math
+        import torch.distributed as dist
+        from . import attention as ab
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.B = len(K_chunks)
+        self.nq, self.nkv, self.hd, self.n = nq, nkv, hd, n_local
+        self.scale = 1.0 / math.sqrt(hd) if scale is None else scale
+        self.softcap = softcap
+        dev = K_chunks[0].device
+        self.rows = self.B * nq
+        self.per = self.rows * (hd + 2)
+        self.send = torch.empty(self.per, dtype=torch.float32, device=dev)
+        self.recv = torch.empty(self.world * self.per, dtype=torch.float32, device=dev)
+        self.out = torch.empty(self.B, nq * hd, dtype=torch.float32, device=dev)
+        self.Kt, self.Vt = ab.ptr_table(list(K_chunks), dev), ab.ptr_table(list(V_chunks), dev)
+        self.lo = torch.zeros(self.B, dtype=torch.int32, device=dev)
+        self.hi = torch.full((self.B,), n_local, dtype=torch.int32, device=dev)
+        nbytes = ab.decode_workspace_size(self.B, nq, nkv, hd, max(1, n_local))
+        self.ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+
+    def __call__(self, q: torch.Tensor, gate: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+        from . import _lib
+        from .attention import GPUError, _stream
+        lib = _lib.load()
+        st = _stream(stream)
+        sp = self.send.data_ptr()
+        rc = lib.aspida_attn_decode_partial(
+            q.data_ptr(), self.Kt.data_ptr(), self.Vt.data_ptr(), self.lo.data_ptr(),
+            self.hi.data_ptr(), sp, sp + 4 * self.rows, sp + 8 * self.rows, self.B, self.nq,
+            self.nkv, self.hd, self.scale, self.softcap, max(1, self.n), 0, self.ws.data_ptr(),
+            self.ws.numel(), st)
+        if rc:
+            raise GPUError(rc, "decode_partial")
+        src = self.send
+        if self.world > 1:
+            import torch.distributed as dist
+            try:
+                dist.all_gather_into_tensor(self.recv, self.send, group=self.group)
+            except Exception as e:  # a peer died, timed out or the group was torn down
+                raise ShardError(f"partial exchange failed: {e}") from e
+            src = self.recv
+        rp = src.data_ptr()
+        rc = lib.aspida_attn_merge_strided(
+            rp, rp + 4 * self.rows, rp + 8 * self.rows, None if gate is None else gate.data_ptr(),
+            self.out.data_ptr(), self.world, self.rows, self.hd, self.per, st)
+        if rc:
+            raise GPUError(rc, "merge_strided")
+        return self.out
+
+
+def seq_parallel_decode(q: torch.Tensor, K_local, V_local, n_local: int, nq: int, nkv: int,
+                        hd: int, *, gate: Optional[torch.Tensor] = None,
+                        scale: Optional[float] = None, softcap: float = 0.0,
+                        group=None) -> torch.Tensor:
+    """One-shot form of :class:`SeqParallelDecode`. q [B, nq*hd] f32 (identical
+    on every rank); K_local / V_local: one tensor when B = 1, else a sequence
+    of B chunks. Returns the merged [B, nq*hd] output on every rank."""
+    Ks = [K_local] if isinstance(K_local, torch.Tensor) else list(K_local)
+    Vs = [V_local] if isinstance(V_local, torch.Tensor) else list(V_local)
+    if len(Ks) != q.shape[0] or len(Vs) != q.shape[0]:
+        raise ValueError("one K/V chunk per sequence")
+    op = SeqParallelDecode(Ks, Vs, n_local, nq, nkv, hd, scale=scale, softcap=softcap,
+                           group=group)
+    return op(q, gate=gate).clone()

@@ -189,6 +189,39 @@ def prefill_leg(ab, torch, dev, seed, steps, warmup, stream):
     return ms, flops, (qs[0], Ks[0], Vs[0])
 
 
+def long_leg(ab, torch, dev, rank, world, steps, warmup, stream, dist):
+    """BASELINE config 5a: one 131072-token sequence, 64/8 heads, hd 128, fp16
+    KV split into contiguous chunks across the ranks; each step = partial
+    (m, l, o) over the local chunk + NCCL all-gather + merge (strong scaling:
+    the total KV is fixed). Returns (ms per step, KV bytes of this rank)."""
+    from aspida_b200 import shard
+    nq, nkv, hd, L = 64, 8, 128, 131072
+    lo, hi = shard.kv_chunks(L, world)[rank]
+    n = hi - lo
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    K = torch.randn(max(n, 1), nkv * hd, generator=g, device=dev).half()
+    V = torch.randn(max(n, 1), nkv * hd, generator=g, device=dev).half()
+    q = torch.randn(1, nq * hd, generator=torch.Generator(device=dev).manual_seed(3000),
+                    device=dev)
+    op = shard.SeqParallelDecode([K], [V], n, nq, nkv, hd)
+
+    def step():
+        op(q, stream=stream)
+
+    for _ in range(max(3, warmup)):
+        step()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps, n * nkv * hd * 2 * 2
+
+
 def prefill_cpu_sample(q, K, V, seconds=8.0):
     """CPU oracle on the last rows of one config-3 sequence (causal flops of
     those rows / time), all host cores."""
@@ -364,20 +397,22 @@ def main():
                                           stream)
     if ab.device_status() != 0:
         raise RuntimeError("device status after prefill")
+    l_ms, l_bytes = long_leg(ab, torch, dev, rank, world, max(10, min(args.steps, 100)),
+                             args.warmup, stream, dist)
 
     nbytes = algo_bytes(lens)
-    stats = torch.tensor([ms, ms_e2e, p_ms, float(nbytes), float(p_flops)], dtype=torch.float64,
-                         device=dev)
+    stats = torch.tensor([ms, ms_e2e, p_ms, l_ms, float(nbytes), float(p_flops), float(l_bytes)],
+                         dtype=torch.float64, device=dev)
     if dist:
-        mx = stats[:3].clone()
+        mx = stats[:4].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = stats[3:].clone()
+        tot = stats[4:].clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms_max, ms_e2e_max, p_ms_max = float(mx[0]), float(mx[1]), float(mx[2])
-        bytes_all, flops_all = float(tot[0]), float(tot[1])
+        ms_max, ms_e2e_max, p_ms_max, l_ms_max = (float(x) for x in mx)
+        bytes_all, flops_all, l_bytes_all = (float(x) for x in tot)
     else:
-        ms_max, ms_e2e_max, p_ms_max = ms, ms_e2e, p_ms
-        bytes_all, flops_all = float(nbytes), float(p_flops)
+        ms_max, ms_e2e_max, p_ms_max, l_ms_max = ms, ms_e2e, p_ms, l_ms
+        bytes_all, flops_all, l_bytes_all = float(nbytes), float(p_flops), float(l_bytes)
 
     if rank == 0:
         hbm, src = peaks()
@@ -423,6 +458,15 @@ def main():
                              "traffic": None,
                              "peak_source": f"{peaks_tensor()[1]} bf16_tflops (cuBLAS, burst)"},
                 "gpu_launches": p_steps,
+            },
+            "decode_long": {
+                "metric": "decode attn KV GB/s (cfg5a: one 131072-token sequence, 64/8 heads, "
+                          "hd128, KV split across GPUs + NCCL (m,l,o) merge)",
+                "value": round(l_bytes_all / (l_ms_max * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(l_ms_max, 5), "scaling": "strong",
+                "kv_bytes_total": int(l_bytes_all),
+                "frac_of_hbm_x_gpus": round(l_bytes_all / (l_ms_max * 1e-3) / 1e9
+                                            / (peaks()[0] * world), 4),
             },
         }
         if world == 1 and not args.no_cpu_baseline:

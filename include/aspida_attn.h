@@ -157,6 +157,14 @@ int aspida_attn_decode_partial(const float* q, const void* const* K, const void*
 int aspida_attn_merge(const float* m, const float* l, const float* o, const float* gate,
                       float* out, int S, int rows, int hd, void* stream);
 
+/* Same merge over partials gathered per rank into one buffer: partial s of
+ * m, l and o starts part_stride floats after partial s-1 (e.g. each rank's
+ * packed [m | l | o] block of an all-gather). No counterpart in the
+ * reference; the strided form spares a copy after the exchange. */
+int aspida_attn_merge_strided(const float* m, const float* l, const float* o, const float* gate,
+                              float* out, int S, int rows, int hd, long part_stride,
+                              void* stream);
+
 /* ------------------------------------------------------------------------
  * Causal prefill attention on the tcgen05 tensor cores.
  * Replaces aspida_ggml_fattn_prefill (gpu/fattn_ggml.cuh:109-141) and the

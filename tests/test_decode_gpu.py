@@ -226,3 +226,16 @@ def test_argument_errors(ab):
     assert e.value.code == ab.ASPIDA_ERR_ARG
     assert ab.last_error() != 0
     assert ab.last_error() == 0
+
+
+def test_seq_parallel_object_single_rank(ab, oracle):
+    """SeqParallelDecode with one rank (no process group): partial + strided
+    merge over the packed buffer equals whole-range decode."""
+    from aspida_b200 import shard
+    nq, nkv, hd, L = 64, 8, 128, 9000
+    q, Ks, Vs = make_batch([L], nq, nkv, hd, seed=12)
+    op = shard.SeqParallelDecode(Ks, Vs, L, nq, nkv, hd)
+    for _ in range(2):
+        out = op(q).cpu().numpy()
+        ref = oracle_decode(oracle, q, Ks, Vs, [L - 1], nq, nkv, hd)
+        assert_parity(out, ref, what="seq-parallel single rank")
