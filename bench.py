@@ -50,7 +50,8 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
-                    help="for ncu: only warm-up + timed decode steps, no clock soak, e2e or CPU legs")
+                    help="for ncu: only warm-up + timed steps of one leg, no clock soak, e2e or CPU")
+    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long"], default="decode")
     return ap.parse_args()
 
 
@@ -336,10 +337,17 @@ def main():
     torch.cuda.synchronize()
 
     if args.profile:
-        for _ in range(args.steps):
-            step()
+        if args.profile_leg == "decode":
+            for _ in range(args.steps):
+                step()
+        elif args.profile_leg == "prefill":
+            for c in caches:
+                c.free()
+            prefill_leg(ab, torch, dev, 2000 + rank, args.steps, args.warmup, stream)
+        else:
+            long_leg(ab, torch, dev, rank, world, args.steps, args.warmup, stream, dist)
         torch.cuda.synchronize()
-        print(json.dumps({"profile_run": True, "steps": args.steps}))
+        print(json.dumps({"profile_run": True, "leg": args.profile_leg, "steps": args.steps}))
         return
     sampler = ClockSampler(local)
     sampler.start()
