@@ -9,7 +9,8 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libaspida_attn.so")
+# ASPIDA_ATTN_LIB overrides the in-tree library (e.g. to load an alternative build)
+LIB_PATH = os.environ.get("ASPIDA_ATTN_LIB") or os.path.join(_HERE, "libaspida_attn.so")
 
 i32, f32, sz, vp = C.c_int, C.c_float, C.c_size_t, C.c_void_p
 pp = C.POINTER(C.c_void_p)

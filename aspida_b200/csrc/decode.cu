@@ -400,8 +400,8 @@ decode_kernel(const DecodeParams p) {
 // has finished and its writes are visible. Sequences with an empty key range
 // (no units) get zeros (mode 0) or an empty partial (mode 1) here.
 template <int HD>
-__global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
-  constexpr int NW = 4, PER = HD / 32;
+__global__ void __launch_bounds__(256) combine_kernel(const DecodeParams p) {
+  constexpr int NW = 8, PER = HD / 32;
   __shared__ float red_o[NW][HD];
   __shared__ float red_m[NW], red_l[NW];
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -436,12 +436,14 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
   for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
   if (lane == 0) red_m[warp] = M;
   __syncthreads();
-  M = fmaxf(fmaxf(red_m[0], red_m[1]), fmaxf(red_m[2], red_m[3]));
+  M = red_m[0];
+#pragma unroll
+  for (int w = 1; w < NW; ++w) M = fmaxf(M, red_m[w]);
 
   float L = 0.f, acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) acc[i] = 0.f;
-#pragma unroll 4
+#pragma unroll 8
   for (long c = ca + warp; c <= cb; c += NW) {
     const long s = (c + seg) * p.hpc + h;
     const float wt = fast_exp2(p.ws_ml[s * 16 + gq * 2] - M);
@@ -462,9 +464,13 @@ __global__ void __launch_bounds__(128) combine_kernel(const DecodeParams p) {
   for (int i = 0; i < PER; ++i) red_o[warp][lane * PER + i] = acc[i];
   if (lane == 0) red_l[warp] = L;
   __syncthreads();
-  L = red_l[0] + red_l[1] + red_l[2] + red_l[3];
+  L = 0.f;
+#pragma unroll
+  for (int w = 0; w < NW; ++w) L += red_l[w];
   for (int d = threadIdx.x; d < HD; d += blockDim.x) {
-    const float v = red_o[0][d] + red_o[1][d] + red_o[2][d] + red_o[3][d];
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) v += red_o[w][d];
     if (p.mode == 0) {
       float r = L > 0.f ? v / L : 0.f;
       if (p.gate) r *= 1.f / (1.f + expf(-p.gate[oi + d]));
@@ -531,7 +537,7 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
   // merges as soon as the decode grid completes
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.B, p.nkv, p.G);
-  cfg.blockDim = dim3(128);
+  cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

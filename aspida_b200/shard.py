@@ -122,6 +122,7 @@ class SeqParallelDecode:
         self.hi = torch.full((self.B,), n_local, dtype=torch.int32, device=dev)
         nbytes = ab.decode_workspace_size(self.B, nq, nkv, hd, max(1, n_local))
         self.ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        self.pos = torch.full((self.B,), n_local - 1, dtype=torch.int32, device=dev)
 
     def __call__(self, q: torch.Tensor, gate: Optional[torch.Tensor] = None,
                  stream=None) -> torch.Tensor:
@@ -129,6 +130,16 @@ class SeqParallelDecode:
         from .attention import GPUError, _stream
         lib = _lib.load()
         st = _stream(stream)
+        if self.world == 1:
+            # one rank holds the whole range: plain decode, no partial round trip
+            rc = lib.aspida_attn_decode(
+                q.data_ptr(), None if gate is None else gate.data_ptr(), self.Kt.data_ptr(),
+                self.Vt.data_ptr(), self.pos.data_ptr(), None, self.out.data_ptr(), self.B,
+                self.nq, self.nkv, self.hd, self.scale, 0, self.softcap, max(1, self.n), 0,
+                self.ws.data_ptr(), self.ws.numel(), st)
+            if rc:
+                raise GPUError(rc, "decode")
+            return self.out
         sp = self.send.data_ptr()
         rc = lib.aspida_attn_decode_partial(
             q.data_ptr(), self.Kt.data_ptr(), self.Vt.data_ptr(), self.lo.data_ptr(),
