@@ -33,6 +33,8 @@ SIGNATURES = {
     "aspida_attn_decode_workspace_size": (sz, [i32, i32, i32, i32, i32, i32]),
     "aspida_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, f32,
                                  i32, i32, vp, sz, vp]),
+    "aspida_attn_decode_paged": (i32, [vp, vp, vp, vp, vp, i32, i32, vp, vp, i32, i32, i32, i32,
+                                       f32, i32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_decode_partial": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
                                          f32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
@@ -43,6 +45,7 @@ SIGNATURES = {
                                   vp]),
     "aspida_attn_prefill_batch": (i32, [i32, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
                                         i32, f32, vp]),
+    "aspida_attn_prefill_gated": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, vp]),
     "aspida_attn_step_host": (i32, [vp, i32, vp, vp, vp, vp, vp, i32, i32, i32, f32, i32, f32,
                                     i32, f32, i32, vp]),
 }

@@ -342,3 +342,26 @@ def prefill_batch(qs, Ks, Vs, nq: int, nkv: int, hd: int, pos_starts=None, *,
         softcap, _stream(stream))
     _check(rc, "prefill_batch")
     return outs
+
+
+def decode_paged(q: torch.Tensor, K_pool: torch.Tensor, V_pool: torch.Tensor,
+                 block_table: torch.Tensor, block_size: int, pos: torch.Tensor, nq: int,
+                 nkv: int, hd: int, *, gate: Optional[torch.Tensor] = None,
+                 scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
+                 max_kv_len: int, chunk: int = 0, out: Optional[torch.Tensor] = None,
+                 workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """Decode over a paged KV pool: K_pool/V_pool fp16 [blocks*block_size,
+    nkv*hd]; block_table int32 [B, max_blocks] of block ids."""
+    B = q.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((B, nq * hd), dtype=torch.float32, device=q.device)
+    nbytes = decode_workspace_size(B, nq, nkv, hd, max_kv_len, chunk)
+    wsb = _ws(workspace, q.device).get(nbytes, q.device)
+    rc = _lib_().aspida_attn_decode_paged(
+        _ptr(q), _ptr(gate), _ptr(K_pool), _ptr(V_pool), _ptr(block_table), block_table.shape[1],
+        block_size, _ptr(pos), _ptr(out), B, nq, nkv, hd, scale, window, softcap, max_kv_len,
+        chunk, _ptr(wsb), wsb.numel(), _stream(stream))
+    _check(rc, "decode_paged")
+    return out

@@ -53,6 +53,10 @@ struct DecodeParams {
   const float* gate;
   const __half* const* K;
   const __half* const* V;
+  const __half* Kpool;  // paged form: shared pools of blocks of block_size rows
+  const __half* Vpool;
+  const int* block_table;   // [B][max_blocks] block ids, or null (per-sequence caches)
+  int block_size, max_blocks;
   const int* pos;       // mode 0
   const int* max_len;   // mode 0, optional
   const int* kv_lo;     // mode 1
@@ -220,8 +224,17 @@ decode_kernel(const DecodeParams p) {
       const int which = lane >> 4;        // 0: K row, 1: V row
       const int r = lane & 15;
       const int key = min(cursor_key0(cur) + r, cur.hi - 1);  // past the end: repeat a valid row
-      const __half* base = which ? p.V[cur.b] : p.K[cur.b];
-      const __half* src = base + (long)key * p.nkv * HD + (long)cur.grp * HPC * HD;
+      const __half* base;
+      long row;
+      if (p.block_table) {            // paged: key -> (block id, row in block)
+        base = which ? p.Vpool : p.Kpool;
+        const int blk = p.block_table[(long)cur.b * p.max_blocks + key / p.block_size];
+        row = (long)blk * p.block_size + key % p.block_size;
+      } else {
+        base = which ? p.V[cur.b] : p.K[cur.b];
+        row = key;
+      }
+      const __half* src = base + row * p.nkv * HD + (long)cur.grp * HPC * HD;
       bulk_g2s(smem + slot * STAGE_BYTES + (which * kKeys + r) * ROWB, src, Geo::SLICE, &full[slot]);
       ++fill;
       ++cur.u;
@@ -563,7 +576,9 @@ int launch_decode_hd(DecodeParams& p, long units_hint, int chunk, cudaStream_t s
 int run_decode(DecodeParams& p, int hd, int max_kv_len, int chunk, void* ws, size_t ws_bytes,
                cudaStream_t st) {
   if (p.B <= 0) return 0;
-  if (p.B > kMaxB || p.nq <= 0 || p.nkv <= 0 || p.nq % p.nkv != 0 || !p.q || !p.K || !p.V ||
+  if (p.B > kMaxB || p.nq <= 0 || p.nkv <= 0 || p.nq % p.nkv != 0 || !p.q ||
+      (p.block_table ? (!p.Kpool || !p.Vpool || p.block_size <= 0 || p.max_blocks <= 0)
+                     : (!p.K || !p.V)) ||
       max_kv_len < 0 || chunk < 0)
     return record_status(ASPIDA_ERR_ARG);
   if (p.G > 8 || (hd != 64 && hd != 128 && hd != 256)) return record_status(ASPIDA_ERR_UNSUPPORTED);
@@ -629,6 +644,25 @@ int decode_with_status(const float* q, const float* gate, const void* const* K,
   return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
 }
 
+int decode_paged(const float* q, const float* gate, const void* K_pool, const void* V_pool,
+                 const int* block_table, int max_blocks, int block_size, const int* pos,
+                 float* out, int B, int nq, int nkv, int hd, float scale, int window,
+                 float softcap, int max_kv_len, int chunk, void* ws, size_t ws_bytes,
+                 cudaStream_t st) {
+  DecodeParams p{};
+  p.q = q; p.gate = gate;
+  p.Kpool = static_cast<const __half*>(K_pool);
+  p.Vpool = static_cast<const __half*>(V_pool);
+  p.block_table = block_table; p.block_size = block_size; p.max_blocks = max_blocks;
+  p.pos = pos; p.out = out;
+  p.B = B; p.nq = nq; p.nkv = nkv; p.G = nkv > 0 ? nq / nkv : 0;
+  p.window = window; p.mode = 0;
+  p.scale_log2 = scale * kLog2e; p.softcap = softcap;
+  if (B > 0 && (!pos || !out || !block_table)) return record_status(ASPIDA_ERR_ARG);
+  if (max_kv_len > (long)max_blocks * block_size) return record_status(ASPIDA_ERR_ARG);
+  return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
+}
+
 int decode_partial(const float* q, const void* const* K, const void* const* V, const int* kv_lo,
                    const int* kv_hi, float* m, float* l, float* o, int B, int nq, int nkv, int hd,
                    float scale, float softcap, int max_kv_len, int chunk, void* ws,
@@ -660,6 +694,17 @@ extern "C" int aspida_attn_decode(const float* q, const float* gate, const void*
                                   void* workspace, size_t workspace_bytes, void* stream) {
   return aspida::decode(q, gate, K, V, pos, max_len, out, B, nq, nkv, hd, scale, window, softcap,
                         max_kv_len, chunk, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_decode_paged(const float* q, const float* gate, const void* K_pool,
+                                        const void* V_pool, const int* block_table,
+                                        int max_blocks, int block_size, const int* pos,
+                                        float* out, int B, int nq, int nkv, int hd, float scale,
+                                        int window, float softcap, int max_kv_len, int chunk,
+                                        void* workspace, size_t workspace_bytes, void* stream) {
+  return aspida::decode_paged(q, gate, K_pool, V_pool, block_table, max_blocks, block_size, pos,
+                              out, B, nq, nkv, hd, scale, window, softcap, max_kv_len, chunk,
+                              workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int aspida_attn_decode_partial(const float* q, const void* const* K,

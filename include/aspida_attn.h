@@ -138,6 +138,20 @@ int aspida_attn_decode(const float* q, const float* gate, const void* const* K,
                        int max_kv_len, int chunk, void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Paged-KV decode: the K and V rows of all sequences live in shared pools of
+ * fixed-size blocks, dev fp16 [num_blocks * block_size][nkv*hd] (block k =
+ * rows k*block_size..); row `key` of sequence b is pool row
+ * block_table[b*max_blocks + key/block_size]*block_size + key%block_size.
+ * Blocks may be shared between sequences (prefix sharing). Arguments as for
+ * aspida_attn_decode otherwise (max_kv_len <= max_blocks*block_size). The
+ * block-table model follows KV_Pool (src/llm/kv_pool.ads:1-47), which the
+ * reference keeps on the host only. */
+int aspida_attn_decode_paged(const float* q, const float* gate, const void* K_pool,
+                             const void* V_pool, const int* block_table, int max_blocks,
+                             int block_size, const int* pos, float* out, int B, int nq, int nkv,
+                             int hd, float scale, int window, float softcap, int max_kv_len,
+                             int chunk, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Split-KV partial for sequence-parallel decode: attend keys
  * kv_lo[b]..kv_hi[b]-1 of each cache and write the unnormalised partial
  * (m = running max in natural-log units, l = sum of exp(s-m), o = sum of
@@ -186,6 +200,16 @@ int aspida_attn_prefill_batch(int nseq, const void* const* q, const void* const*
                               const void* const* V, const float* const* gate, void* const* out,
                               const int* P, const int* pos_start, int out_f32, int nq, int nkv,
                               int hd, float scale, int window, float softcap, void* stream);
+
+/* Qwen gated prefill with the argument list of the shim's internal swap
+ * point aspida_ggml_fattn_prefill (gpu/fattn_ggml.cuh:109-112), which it
+ * replaces: q_all dev f32 [P][nq*hd] (prepped, 16-byte aligned), K/V dev
+ * fp16 cache [>= pos_start+P][nkv*hd], gate dev f32 [P][nq*hd] or NULL,
+ * out dev f32 [P][nq*hd]; scale 1/sqrt(hd); causal. Returns 0 (the shim's
+ * `true`) or an error, in which case `out` is zeroed as the shim does. */
+int aspida_attn_prefill_gated(const float* q_all, const void* K, const void* V, const float* gate,
+                              float* out, int nq, int nkv, int hd, int P, int pos_start,
+                              void* stream);
 
 /* Host-buffer decode step for B resident states — the attention half of
  * aspida_gpu_fattn_step / chain_forward_batch (gpu/gpu_matvec.cu:1613, 2783)

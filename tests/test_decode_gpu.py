@@ -239,3 +239,36 @@ def test_seq_parallel_object_single_rank(ab, oracle):
         out = op(q).cpu().numpy()
         ref = oracle_decode(oracle, q, Ks, Vs, [L - 1], nq, nkv, hd)
         assert_parity(out, ref, what="seq-parallel single rank")
+
+
+def test_decode_paged_matches_contiguous(ab, oracle):
+    """Paged KV (block tables over a shared pool, blocks shared between
+    sequences as in prefix sharing) gives the same output as contiguous caches."""
+    nq, nkv, hd, bs = 32, 8, 128, 64
+    lens = [1, 63, 64, 65, 1000, 3001]
+    rng = np.random.RandomState(31)
+    nblk = [(L + bs - 1) // bs for L in lens]
+    max_blocks = max(nblk)
+    total = sum(nblk) + 3
+    perm = rng.permutation(total)                     # scattered block placement
+    g = torch.Generator(device="cuda").manual_seed(31)
+    Kpool = torch.randn(total * bs, nkv * hd, generator=g, device="cuda").half()
+    Vpool = torch.randn(total * bs, nkv * hd, generator=g, device="cuda").half()
+    table = np.zeros((len(lens), max_blocks), np.int32)
+    k = 0
+    for b, n in enumerate(nblk):
+        table[b, :n] = perm[k:k + n]
+        k += n
+    table[5, 0] = table[4, 0]                         # shared first block (common prefix)
+    Ks, Vs = [], []
+    for b, L in enumerate(lens):
+        rows = np.concatenate([np.arange(t * bs, t * bs + bs) for t in table[b, :nblk[b]]])[:L]
+        Ks.append(Kpool[torch.from_numpy(rows).long().cuda()])
+        Vs.append(Vpool[torch.from_numpy(rows).long().cuda()])
+    q = torch.randn(len(lens), nq * hd, generator=g, device="cuda")
+    pos = torch.tensor([L - 1 for L in lens], dtype=torch.int32, device="cuda")
+    got = ab.decode_paged(q, Kpool, Vpool, torch.from_numpy(table).cuda(), bs, pos, nq, nkv, hd,
+                          max_kv_len=max(lens))
+    torch.cuda.synchronize()
+    ref = oracle_decode(oracle, q, Ks, Vs, [L - 1 for L in lens], nq, nkv, hd)
+    assert_parity(got.cpu().numpy(), ref, what="paged")

@@ -87,3 +87,34 @@ def test_prefill_batch_cfg3_rows(ab, oracle):
     for b in range(4):
         ref = oracle_prefill(oracle, qs[b], Ks[b], Vs[b], 0, nq, nkv, hd, rows=rows)
         assert_parity(outs[b].cpu().numpy()[rows], ref[rows], what=f"cfg3 seq {b}")
+
+
+def test_gated_prefill_exact_signature_hura_dims(ab, oracle):
+    """The Qwen gated path at the production dims (16 q / 2 kv heads, hd 256)
+    through aspida_attn_prefill_gated, the drop-in for the shim's
+    aspida_ggml_fattn_prefill: f32 queries, sigmoid gate, f32 output, chunked
+    (pos_start > 0)."""
+    from aspida_b200 import _lib
+    nq, nkv, hd, P, ps = 16, 2, 256, 300, 200
+    g = torch.Generator(device="cuda").manual_seed(41)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda")
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    gate = torch.randn(P, nq * hd, generator=g, device="cuda")
+    out = torch.full((P, nq * hd), float("nan"), device="cuda")
+    rc = _lib.load().aspida_attn_prefill_gated(q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                               gate.data_ptr(), out.data_ptr(), nq, nkv, hd, P,
+                                               ps, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    ref = oracle.prefill(q.cpu().numpy(), K.float().cpu().numpy(), V.float().cpu().numpy(), ps,
+                         nq, nkv, hd, gate=gate.cpu().numpy())
+    assert_parity(out.cpu().numpy(), ref, what="gated prefill")
+    # an unsupported head dim fails and zeroes the output, as the shim does
+    bad = torch.full((4, 4 * 96), 1.0, device="cuda")
+    rc = _lib.load().aspida_attn_prefill_gated(bad.data_ptr(), K.data_ptr(), V.data_ptr(), None,
+                                               bad.data_ptr(), 4, 1, 96, 4, 0,
+                                               torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == ab.ASPIDA_ERR_UNSUPPORTED and float(bad.abs().max()) == 0.0
+    ab.last_error()
