@@ -37,6 +37,9 @@ SIGNATURES = {
                                        f32, i32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_decode_partial": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
                                          f32, f32, i32, i32, vp, sz, vp]),
+    "aspida_attn_decode_q8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
+                                    i32, f32, i32, i32, vp, sz, vp]),
+    "aspida_attn_quantize_q8": (i32, [vp, vp, vp, C.c_longlong, vp]),
     "aspida_attn_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "aspida_attn_merge_strided": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, C.c_long, vp]),
     "aspida_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32,

@@ -243,6 +243,50 @@ def decode(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor, pos: torch
     return out
 
 
+def quantize_q8(x: torch.Tensor, q: Optional[torch.Tensor] = None,
+                scales: Optional[torch.Tensor] = None, stream=None):
+    """Q8_0-quantise f32 x [..., n] (n a multiple of 32) into int8 q [..., n]
+    and fp16 scales [..., n/32] (k_to_q8, gpu/fattn_kvhalf.cu:143-152).
+    q / scales may be views into a cache (rows being appended)."""
+    if x.dtype != torch.float32 or not x.is_contiguous() or x.shape[-1] % 32:
+        raise ValueError("x must be contiguous f32 with a last dim divisible by 32")
+    if q is None:
+        q = torch.empty(x.shape, dtype=torch.int8, device=x.device)
+    if scales is None:
+        scales = torch.empty((*x.shape[:-1], x.shape[-1] // 32), dtype=torch.float16,
+                             device=x.device)
+    if q.numel() != x.numel() or scales.numel() * 32 != x.numel() or not q.is_contiguous() \
+            or not scales.is_contiguous():
+        raise ValueError("q / scales do not match x")
+    rc = _lib_().aspida_attn_quantize_q8(_ptr(x), _ptr(q), _ptr(scales), x.numel() // 32,
+                                         _stream(stream))
+    _check(rc, "quantize_q8")
+    return q, scales
+
+
+def decode_q8(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor, Ks_tab: torch.Tensor,
+              Vs_tab: torch.Tensor, pos: torch.Tensor, nq: int, nkv: int, hd: int, *,
+              gate: Optional[torch.Tensor] = None, max_len: Optional[torch.Tensor] = None,
+              scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
+              max_kv_len: int, chunk: int = 0, out: Optional[torch.Tensor] = None,
+              workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """Batched GQA decode over Q8_0 caches: K_tab/V_tab pointer tables of int8
+    caches [rows, nkv*hd], Ks_tab/Vs_tab of fp16 scales [rows, nkv*hd/32]."""
+    B = q.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((B, nq * hd), dtype=torch.float32, device=q.device)
+    nbytes = decode_workspace_size(B, nq, nkv, hd, max_kv_len, chunk)
+    wsb = _ws(workspace, q.device).get(nbytes, q.device)
+    rc = _lib_().aspida_attn_decode_q8(
+        _ptr(q), _ptr(gate), _ptr(K_tab), _ptr(V_tab), _ptr(Ks_tab), _ptr(Vs_tab), _ptr(pos),
+        _ptr(max_len), _ptr(out), B, nq, nkv, hd, scale, window, softcap, max_kv_len, chunk,
+        _ptr(wsb), wsb.numel(), _stream(stream))
+    _check(rc, "decode_q8")
+    return out
+
+
 def decode_partial(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor,
                    kv_lo: torch.Tensor, kv_hi: torch.Tensor, nq: int, nkv: int, hd: int, *,
                    scale: Optional[float] = None, softcap: float = 0.0, max_kv_len: int,

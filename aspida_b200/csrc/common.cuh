@@ -122,6 +122,12 @@ __device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t 
 }
 
 // 8x8 b16 transpose across the warp (fragment layout: row lane/4, cols 2*(lane%4)+{0,1}).
+__device__ __forceinline__ uint32_t lds_u32(uint32_t saddr) {
+  uint32_t v;
+  asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));
+  return v;
+}
+
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));

@@ -47,12 +47,20 @@ constexpr int kSmemBudget = 210 * 1024;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kNegBig = -3.402823466e38f;
+// Q8_0 path: P x (V scale) is carried x 64 in fp16 so that small products
+// stay normal; undone when a piece finishes. Safe for scales up to 1023
+// (|v| up to ~130k before quantisation).
+constexpr float kVScale = 64.f;
 
 struct DecodeParams {
   const float* q;
   const float* gate;
   const __half* const* K;
   const __half* const* V;
+  const int8_t* const* K8;    // Q8_0 form: int8 caches [rows][nkv*hd] ...
+  const int8_t* const* V8;
+  const __half* const* Ks;    // ... and fp16 scales [rows][nkv*hd/32]
+  const __half* const* Vs;
   const __half* Kpool;  // paged form: shared pools of blocks of block_size rows
   const __half* Vpool;
   const int* block_table;   // [B][max_blocks] block ids, or null (per-sequence caches)
@@ -157,20 +165,42 @@ __device__ __forceinline__ int cursor_key0(const Cursor& c) {
   return c.lo + (int)(c.u - c.seg_u0) * kKeys;
 }
 
-template <int HD, int HPC>
+template <int HD, int HPC, bool Q8>
 struct Geometry {
-  static constexpr int SLICE = HPC * HD * 2;             // bytes of one row's group slice
-  static constexpr int ROWB = SLICE + 16;                // padded smem row (conflict-free ldmatrix)
-  static constexpr int STAGE_BYTES = 2 * kKeys * ROWB;   // 16 K rows + 16 V rows
+  static constexpr int SLICE = HPC * HD * (Q8 ? 1 : 2);  // bytes of one row's group slice
+  static constexpr int ROWB = SLICE + 16;                // padded smem row (conflict-free reads)
+  static constexpr int SSL = Q8 ? HPC * HD / 16 : 0;     // bytes of one row's group scales
+  static constexpr int STAGE_BYTES = 2 * kKeys * ROWB + 2 * kKeys * SSL;
   static constexpr int STAGES_RAW = (kSmemBudget - (kMaxB + 1) * 4) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int THREADS = (HPC + 1) * 32;
+  static constexpr int STAGE_TX = 2 * kKeys * (SLICE + SSL);  // bytes the copies bring per stage
 };
 
-template <int HD, int HPC>
-__global__ void __launch_bounds__(Geometry<HD, HPC>::THREADS, 1)
+// int8 -> fp16 helpers for the Q8_0 path. A byte b of a word pre-xored with
+// 0x80808080 holds b + 128; placed in the low byte of an fp16 whose high byte
+// is 0x64 it reads 1024 + b + 128, exact, so subtracting 1152 gives b exactly.
+__device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t biased, uint32_t sel) {
+  const uint32_t x = __byte_perm(biased, 0x64646464u, sel);
+  __half2 h = *reinterpret_cast<const __half2*>(&x);
+  h = __hsub2(h, __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Output dimension of accumulator element j of M tile mt. fp16 path: tile mt
+// covers dims 16mt..16mt+15 in order. Q8 path: the two tiles of 32-dim block
+// mt/2 interleave so that lane group g owns dims 4g..4g+3 of the block
+// (rows g, g+8 of tile 2i -> dims 4g, 4g+1; of tile 2i+1 -> 4g+2, 4g+3).
+template <bool Q8>
+__device__ __forceinline__ int out_dim(int mt, int j, int g) {
+  if constexpr (Q8) return (mt >> 1) * 32 + 4 * g + (mt & 1) * 2 + (j >> 1);
+  else return mt * 16 + g + (j >> 1) * 8;
+}
+
+template <int HD, int HPC, bool Q8>
+__global__ void __launch_bounds__(Geometry<HD, HPC, Q8>::THREADS, 1)
 decode_kernel(const DecodeParams p) {
-  using Geo = Geometry<HD, HPC>;
+  using Geo = Geometry<HD, HPC, Q8>;
   constexpr int ROWB = Geo::ROWB, STAGE_BYTES = Geo::STAGE_BYTES, STAGES = Geo::STAGES;
   constexpr int KT = HD / 16;   // 16-dim steps
   extern __shared__ __align__(128) unsigned char smem[];
@@ -219,23 +249,34 @@ decode_kernel(const DecodeParams p) {
           break;   // consumers drain what is in flight, then also stop
         }
       }
-      if (lane == 0) mbar_arrive_expect_tx(&full[slot], 2 * kKeys * Geo::SLICE);
+      if (lane == 0) mbar_arrive_expect_tx(&full[slot], Geo::STAGE_TX);
       __syncwarp();
       const int which = lane >> 4;        // 0: K row, 1: V row
       const int r = lane & 15;
       const int key = min(cursor_key0(cur) + r, cur.hi - 1);  // past the end: repeat a valid row
-      const __half* base;
-      long row;
-      if (p.block_table) {            // paged: key -> (block id, row in block)
-        base = which ? p.Vpool : p.Kpool;
-        const int blk = p.block_table[(long)cur.b * p.max_blocks + key / p.block_size];
-        row = (long)blk * p.block_size + key % p.block_size;
+      unsigned char* dst = smem + slot * STAGE_BYTES;
+      if constexpr (Q8) {
+        const int8_t* base = which ? p.V8[cur.b] : p.K8[cur.b];
+        const __half* sbase = which ? p.Vs[cur.b] : p.Ks[cur.b];
+        bulk_g2s(dst + (which * kKeys + r) * ROWB,
+                 base + (long)key * p.nkv * HD + (long)cur.grp * HPC * HD, Geo::SLICE, &full[slot]);
+        bulk_g2s(dst + 2 * kKeys * ROWB + (which * kKeys + r) * Geo::SSL,
+                 sbase + (long)key * (p.nkv * HD / 32) + (long)cur.grp * (HPC * HD / 32), Geo::SSL,
+                 &full[slot]);
       } else {
-        base = which ? p.V[cur.b] : p.K[cur.b];
-        row = key;
+        const __half* base;
+        long row;
+        if (p.block_table) {            // paged: key -> (block id, row in block)
+          base = which ? p.Vpool : p.Kpool;
+          const int blk = p.block_table[(long)cur.b * p.max_blocks + key / p.block_size];
+          row = (long)blk * p.block_size + key % p.block_size;
+        } else {
+          base = which ? p.V[cur.b] : p.K[cur.b];
+          row = key;
+        }
+        const __half* src = base + row * p.nkv * HD + (long)cur.grp * HPC * HD;
+        bulk_g2s(dst + (which * kKeys + r) * ROWB, src, Geo::SLICE, &full[slot]);
       }
-      const __half* src = base + row * p.nkv * HD + (long)cur.grp * HPC * HD;
-      bulk_g2s(smem + slot * STAGE_BYTES + (which * kKeys + r) * ROWB, src, Geo::SLICE, &full[slot]);
       ++fill;
       ++cur.u;
       cursor_seek(p, pref, cur);
@@ -263,11 +304,19 @@ decode_kernel(const DecodeParams p) {
       const float* qb = p.q + ((long)cur.b * p.nq + (long)kvh * p.G) * HD;
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
-        const int d = kt * 16 + qc;
+        // fp16 path: B rows k (2t, 2t+1 | 2t+8, 2t+9) are dims (qc, qc+1 |
+        // qc+8, qc+9) of the step; Q8 path: dims (4t, 4t+1 | 4t+2, 4t+3)
         float2 a = make_float2(0.f, 0.f), c = make_float2(0.f, 0.f);
         if (g < p.G) {
-          a = *reinterpret_cast<const float2*>(qb + g * HD + d);
-          c = *reinterpret_cast<const float2*>(qb + g * HD + d + 8);
+          if constexpr (Q8) {
+            const float4 f = *reinterpret_cast<const float4*>(qb + g * HD + kt * 16 + 2 * qc);
+            a = make_float2(f.x, f.y);
+            c = make_float2(f.z, f.w);
+          } else {
+            const int d = kt * 16 + qc;
+            a = *reinterpret_cast<const float2*>(qb + g * HD + d);
+            c = *reinterpret_cast<const float2*>(qb + g * HD + d + 8);
+          }
         }
         const __half2 ah = __floats2half2_rn(a.x, a.y), ch = __floats2half2_rn(c.x, c.y);
         const float2 ar = __half22float2(ah), cr = __half22float2(ch);
@@ -286,17 +335,51 @@ decode_kernel(const DecodeParams p) {
       if (lane == 0 && p.status) { atomicExch(&p.status->code, kDevTimeoutMbar); p.status->where = 11; }
       return;
     }
-    const unsigned char* st = smem + slot * STAGE_BYTES + h * HD * 2;
+    const unsigned char* st = smem + slot * STAGE_BYTES + h * HD * (Q8 ? 1 : 2);
     const uint32_t kbase = smem_u32(st), vbase = smem_u32(st + kKeys * ROWB);
+    [[maybe_unused]] const __half* ksc = nullptr;
+    [[maybe_unused]] const __half* vsc = nullptr;
 
-    // S^T = K (Q_hi + Q_lo)^T for 16 keys x 8 query columns
     float s4[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (Q8) {
+      // per 32-dim block: integer K (exact in fp16) times Q, then the block's
+      // per-key scale in f32
+      const unsigned char* sc = smem + slot * STAGE_BYTES + 2 * kKeys * ROWB + h * (HD / 16);
+      ksc = reinterpret_cast<const __half*>(sc);
+      vsc = reinterpret_cast<const __half*>(sc + kKeys * Geo::SSL);
+      const int t = lane & 3;
 #pragma unroll
-    for (int kt = 0; kt < KT; ++kt) {
-      uint32_t a[4];
-      ldmatrix_x4(a[0], a[1], a[2], a[3], kbase + krow * ROWB + (kt * 16 + kcol) * 2);
-      mma_16816(s4, a, qlo[kt][0], qlo[kt][1]);
-      mma_16816(s4, a, qhi[kt][0], qhi[kt][1]);
+      for (int blk = 0; blk < HD / 32; ++blk) {
+        float sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < 2; ++kk) {
+          const int kt = 2 * blk + kk;
+          const uint32_t w0 = lds_u32(kbase + g * ROWB + kt * 16 + 4 * t) ^ 0x80808080u;
+          const uint32_t w1 = lds_u32(kbase + (g + 8) * ROWB + kt * 16 + 4 * t) ^ 0x80808080u;
+          uint32_t a[4];
+          a[0] = i8pair_to_h2(w0, 0x4140);
+          a[1] = i8pair_to_h2(w1, 0x4140);
+          a[2] = i8pair_to_h2(w0, 0x4342);
+          a[3] = i8pair_to_h2(w1, 0x4342);
+          mma_16816(sb, a, qlo[kt][0], qlo[kt][1]);
+          mma_16816(sb, a, qhi[kt][0], qhi[kt][1]);
+        }
+        const float c0 = __half2float(ksc[g * (Geo::SSL / 2) + blk]);
+        const float c1 = __half2float(ksc[(g + 8) * (Geo::SSL / 2) + blk]);
+        s4[0] = fmaf(c0, sb[0], s4[0]);
+        s4[1] = fmaf(c0, sb[1], s4[1]);
+        s4[2] = fmaf(c1, sb[2], s4[2]);
+        s4[3] = fmaf(c1, sb[3], s4[3]);
+      }
+    } else {
+      // S^T = K (Q_hi + Q_lo)^T for 16 keys x 8 query columns
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+        uint32_t a[4];
+        ldmatrix_x4(a[0], a[1], a[2], a[3], kbase + krow * ROWB + (kt * 16 + kcol) * 2);
+        mma_16816(s4, a, qlo[kt][0], qlo[kt][1]);
+        mma_16816(s4, a, qhi[kt][0], qhi[kt][1]);
+      }
     }
     // scale (+ softcap), mask keys past the segment's end
     const int key0 = cursor_key0(cur);
@@ -327,14 +410,47 @@ decode_kernel(const DecodeParams p) {
       oacc[kt][0] *= c0; oacc[kt][1] *= c1;
       oacc[kt][2] *= c0; oacc[kt][3] *= c1;
     }
-    // P^T operand via in-register transpose, then O^T += V^T P^T
-    const uint32_t b0 = movmatrix_trans(pack_half2(p0, p1));
-    const uint32_t b1 = movmatrix_trans(pack_half2(p2, p3));
+    if constexpr (Q8) {
+      // Per 32-dim block: P times the block's per-key V scale (and kVScale),
+      // transposed into the B operand; V^T as exact integers from four
+      // 4-byte reads (keys 2t, 2t+1, 2t+8, 2t+9 at dims 4g..4g+3).
+      const int t = lane & 3;
 #pragma unroll
-    for (int mt = 0; mt < KT; ++mt) {
-      uint32_t a[4];
-      ldmatrix_x4_trans(a[0], a[1], a[2], a[3], vbase + vrow * ROWB + (mt * 16 + vcol) * 2);
-      mma_16816(oacc[mt], a, b0, b1);
+      for (int blk = 0; blk < HD / 32; ++blk) {
+        const float v0 = __half2float(vsc[g * (Geo::SSL / 2) + blk]) * kVScale;
+        const float v1 = __half2float(vsc[(g + 8) * (Geo::SSL / 2) + blk]) * kVScale;
+        const uint32_t b0 = movmatrix_trans(pack_half2(p0 * v0, p1 * v0));
+        const uint32_t b1 = movmatrix_trans(pack_half2(p2 * v1, p3 * v1));
+        const uint32_t col = vbase + blk * 32 + 4 * g;
+        const uint32_t x0 = lds_u32(col + (2 * t) * ROWB) ^ 0x80808080u;
+        const uint32_t x1 = lds_u32(col + (2 * t + 1) * ROWB) ^ 0x80808080u;
+        const uint32_t x2 = lds_u32(col + (2 * t + 8) * ROWB) ^ 0x80808080u;
+        const uint32_t x3 = lds_u32(col + (2 * t + 9) * ROWB) ^ 0x80808080u;
+        // byte-interleave rows: lo = dims 0,1 of both keys, hi = dims 2,3
+        const uint32_t l01 = __byte_perm(x0, x1, 0x5140), h01 = __byte_perm(x0, x1, 0x7362);
+        const uint32_t l23 = __byte_perm(x2, x3, 0x5140), h23 = __byte_perm(x2, x3, 0x7362);
+        uint32_t a[4];
+        a[0] = i8pair_to_h2(l01, 0x4140);  // dim 4g   (tile 2blk row g),   keys 2t, 2t+1
+        a[1] = i8pair_to_h2(l01, 0x4342);  // dim 4g+1 (tile 2blk row g+8)
+        a[2] = i8pair_to_h2(l23, 0x4140);  // dim 4g,   keys 2t+8, 2t+9
+        a[3] = i8pair_to_h2(l23, 0x4342);
+        mma_16816(oacc[2 * blk], a, b0, b1);
+        a[0] = i8pair_to_h2(h01, 0x4140);  // dims 4g+2, 4g+3 (tile 2blk+1)
+        a[1] = i8pair_to_h2(h01, 0x4342);
+        a[2] = i8pair_to_h2(h23, 0x4140);
+        a[3] = i8pair_to_h2(h23, 0x4342);
+        mma_16816(oacc[2 * blk + 1], a, b0, b1);
+      }
+    } else {
+      // P^T operand via in-register transpose, then O^T += V^T P^T
+      const uint32_t b0 = movmatrix_trans(pack_half2(p0, p1));
+      const uint32_t b1 = movmatrix_trans(pack_half2(p2, p3));
+#pragma unroll
+      for (int mt = 0; mt < KT; ++mt) {
+        uint32_t a[4];
+        ldmatrix_x4_trans(a[0], a[1], a[2], a[3], vbase + vrow * ROWB + (mt * 16 + vcol) * 2);
+        mma_16816(oacc[mt], a, b0, b1);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);   // slot may be refilled
@@ -348,6 +464,12 @@ decode_kernel(const DecodeParams p) {
         l0 += __shfl_xor_sync(0xffffffffu, l0, o);
         l1 += __shfl_xor_sync(0xffffffffu, l1, o);
       }
+      if constexpr (Q8) {
+#pragma unroll
+        for (int mt = 0; mt < KT; ++mt)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) oacc[mt][j] *= 1.f / kVScale;
+      }
       const bool whole = cur.seg_u0 >= u_begin && cur.seg_u1 <= u_end;
       const int h0 = kvh * p.G + qc;
       if (whole) {
@@ -358,7 +480,7 @@ decode_kernel(const DecodeParams p) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             if (qc + (j & 1) >= p.G) continue;
-            const int dim = mt * 16 + g + (j >> 1) * 8;
+            const int dim = out_dim<Q8>(mt, j, g);
             const long idx = ob + (long)(h0 + (j & 1)) * HD + dim;
             if (p.mode == 0) {
               float v = oacc[mt][j] * ((j & 1) ? inv1 : inv0);
@@ -388,7 +510,7 @@ decode_kernel(const DecodeParams p) {
         for (int mt = 0; mt < KT; ++mt) {
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const int dim = mt * 16 + g + (j >> 1) * 8;
+            const int dim = out_dim<Q8>(mt, j, g);
             wo[(qc + (j & 1)) * HD + dim] = oacc[mt][j];
           }
         }
@@ -499,20 +621,24 @@ __global__ void __launch_bounds__(256) combine_kernel(const DecodeParams p) {
 }
 
 // kv heads per CTA: the largest of 8/4/2/1 that divides nkv with a group
-// slice of at most 1024 halves (2 KB per row).
-int heads_per_cta(int nkv, int hd) {
-  for (int h : {8, 4, 2, 1})
-    if (nkv % h == 0 && h * hd <= 1024) return h;
-  return 1;
+// slice of at most 1024 halves (2 KB per row). Q8_0 caches: the same head
+// count bound, and a slice of at least 256 bytes so that a row's group scales
+// are a whole number of 16-byte units for the bulk copy (0 = no such split).
+int heads_per_cta(int nkv, int hd, bool q8 = false) {
+  for (int h : {8, 4, 2, 1}) {
+    if (nkv % h != 0) continue;
+    if (!q8 && h * hd <= 1024) return h;
+    if (q8 && h * hd <= 1024 && (h * hd) % 256 == 0) return h;
+  }
+  return q8 ? 0 : 1;
 }
 
 long max_ctas() { return (long)num_sms(); }
 
 struct WsLayout { size_t pref, ml, o, total; long slots; };
 
-WsLayout ws_layout(int B, int nkv, int hd) {
+WsLayout ws_layout(int B, int nkv, int hd, int hpc) {
   WsLayout w;
-  const int hpc = heads_per_cta(nkv, hd);
   w.slots = max_ctas() + (long)B * (nkv / hpc);
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   w.pref = 0;
@@ -522,11 +648,11 @@ WsLayout ws_layout(int B, int nkv, int hd) {
   return w;
 }
 
-template <int HD, int HPC>
+template <int HD, int HPC, bool Q8>
 int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st) {
-  using Geo = Geometry<HD, HPC>;
+  using Geo = Geometry<HD, HPC, Q8>;
   const size_t smem = (size_t)Geo::STAGES * Geo::STAGE_BYTES + (size_t)(p.B + 1) * sizeof(int);
-  auto kern = decode_kernel<HD, HPC>;
+  auto kern = decode_kernel<HD, HPC, Q8>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -565,11 +691,19 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
 
 template <int HD>
 int launch_decode_hd(DecodeParams& p, long units_hint, int chunk, cudaStream_t st) {
+  if (p.K8) {
+    switch (heads_per_cta(p.nkv, HD, true)) {
+      case 8: return launch_decode_v<HD, (HD <= 128 ? 8 : 4), true>(p, units_hint, chunk, st);
+      case 4: return launch_decode_v<HD, 4, true>(p, units_hint, chunk, st);
+      case 2: return launch_decode_v<HD, (HD >= 128 ? 2 : 4), true>(p, units_hint, chunk, st);
+      default: return launch_decode_v<HD, (HD == 256 ? 1 : 4), true>(p, units_hint, chunk, st);
+    }
+  }
   switch (heads_per_cta(p.nkv, HD)) {
-    case 8: return launch_decode_v<HD, (HD <= 128 ? 8 : 4)>(p, units_hint, chunk, st);
-    case 4: return launch_decode_v<HD, 4>(p, units_hint, chunk, st);
-    case 2: return launch_decode_v<HD, 2>(p, units_hint, chunk, st);
-    default: return launch_decode_v<HD, 1>(p, units_hint, chunk, st);
+    case 8: return launch_decode_v<HD, (HD <= 128 ? 8 : 4), false>(p, units_hint, chunk, st);
+    case 4: return launch_decode_v<HD, 4, false>(p, units_hint, chunk, st);
+    case 2: return launch_decode_v<HD, 2, false>(p, units_hint, chunk, st);
+    default: return launch_decode_v<HD, 1, false>(p, units_hint, chunk, st);
   }
 }
 
@@ -578,13 +712,16 @@ int run_decode(DecodeParams& p, int hd, int max_kv_len, int chunk, void* ws, siz
   if (p.B <= 0) return 0;
   if (p.B > kMaxB || p.nq <= 0 || p.nkv <= 0 || p.nq % p.nkv != 0 || !p.q ||
       (p.block_table ? (!p.Kpool || !p.Vpool || p.block_size <= 0 || p.max_blocks <= 0)
+       : p.K8        ? (!p.V8 || !p.Ks || !p.Vs)
                      : (!p.K || !p.V)) ||
       max_kv_len < 0 || chunk < 0)
     return record_status(ASPIDA_ERR_ARG);
   if (p.G > 8 || (hd != 64 && hd != 128 && hd != 256)) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  if (p.K8 && heads_per_cta(p.nkv, hd, true) == 0) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  const int hpc = heads_per_cta(p.nkv, hd, p.K8 != nullptr);
   const long units_hint = (long)p.B * p.nkv * ((std::max(1, max_kv_len) + kKeys - 1) / kKeys);
   if (units_hint >= (1L << 31)) return record_status(ASPIDA_ERR_UNSUPPORTED);
-  WsLayout w = ws_layout(p.B, p.nkv, hd);
+  WsLayout w = ws_layout(p.B, p.nkv, hd, hpc);
   if (!ws || ws_bytes < w.total) return record_status(ASPIDA_ERR_WORKSPACE);
   if (((uintptr_t)ws & 255) != 0) return record_status(ASPIDA_ERR_ARG);
   unsigned char* wb = static_cast<unsigned char*>(ws);
@@ -594,9 +731,9 @@ int run_decode(DecodeParams& p, int hd, int max_kv_len, int chunk, void* ws, siz
   p.slots = w.slots;
   if (!p.status) p.status = device_status_ptr();
   switch (hd) {
-    case 64: return launch_decode_hd<64>(p, units_hint / heads_per_cta(p.nkv, 64), chunk, st);
-    case 128: return launch_decode_hd<128>(p, units_hint / heads_per_cta(p.nkv, 128), chunk, st);
-    default: return launch_decode_hd<256>(p, units_hint / heads_per_cta(p.nkv, 256), chunk, st);
+    case 64: return launch_decode_hd<64>(p, units_hint / hpc, chunk, st);
+    case 128: return launch_decode_hd<128>(p, units_hint / hpc, chunk, st);
+    default: return launch_decode_hd<256>(p, units_hint / hpc, chunk, st);
   }
 }
 
@@ -605,7 +742,10 @@ int run_decode(DecodeParams& p, int hd, int max_kv_len, int chunk, void* ws, siz
 size_t decode_workspace_size(int B, int nq, int nkv, int hd, int max_kv_len, int chunk) {
   (void)nq; (void)max_kv_len; (void)chunk;
   if (B <= 0 || nkv <= 0) return 0;
-  return ws_layout(B, nkv, hd).total;
+  // one size serves the fp16 and the Q8_0 caches
+  size_t n = ws_layout(B, nkv, hd, heads_per_cta(nkv, hd)).total;
+  if (const int h8 = heads_per_cta(nkv, hd, true)) n = std::max(n, ws_layout(B, nkv, hd, h8).total);
+  return n;
 }
 
 int decode(const float* q, const float* gate, const void* const* K, const void* const* V,
@@ -680,7 +820,91 @@ int decode_partial(const float* q, const void* const* K, const void* const* V, c
   return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
 }
 
+int decode_q8(const float* q, const float* gate, const void* const* K8, const void* const* V8,
+              const void* const* Ks, const void* const* Vs, const int* pos, const int* max_len,
+              float* out, int B, int nq, int nkv, int hd, float scale, int window, float softcap,
+              int max_kv_len, int chunk, void* ws, size_t ws_bytes, cudaStream_t st) {
+  DecodeParams p{};
+  p.q = q; p.gate = gate;
+  p.K8 = reinterpret_cast<const int8_t* const*>(K8);
+  p.V8 = reinterpret_cast<const int8_t* const*>(V8);
+  p.Ks = reinterpret_cast<const __half* const*>(Ks);
+  p.Vs = reinterpret_cast<const __half* const*>(Vs);
+  p.pos = pos; p.max_len = max_len; p.out = out;
+  p.B = B; p.nq = nq; p.nkv = nkv; p.G = nkv > 0 ? nq / nkv : 0;
+  p.window = window; p.mode = 0;
+  p.scale_log2 = scale * kLog2e; p.softcap = softcap;
+  if (B > 0 && (!pos || !out || !K8)) return record_status(ASPIDA_ERR_ARG);
+  return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
+}
+
+// Q8_0 quantiser: the algorithm of k_to_q8 (gpu/fattn_kvhalf.cu:143-152).
+// Each 32-value block gets d = max|v| / 127 (stored as fp16) and values
+// round-to-nearest(v * (1/d)) clamped to [-127, 127]; an all-zero block gets
+// d = 0 and zeros. One thread per block; a warp covers 32 consecutive blocks.
+__global__ void quantize_q8_kernel(const float* __restrict__ in, int8_t* __restrict__ q,
+                                   __half* __restrict__ sc, long nblk) {
+  const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nblk) return;
+  const float4* v4 = reinterpret_cast<const float4*>(in + b * 32);
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 t = v4[i];
+    v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const float d = __fdiv_rn(amax, 127.f);
+  const float id = d > 0.f ? __fdiv_rn(1.f, d) : 0.f;
+  sc[b] = __float2half_rn(d);
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t x = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int qi = max(-127, min(127, __float2int_rn(__fmul_rn(v[4 * i + k], id))));
+      x |= (uint32_t)(qi & 0xff) << (8 * k);
+    }
+    w[i] = x;
+  }
+  uint4* qo = reinterpret_cast<uint4*>(q + b * 32);
+  qo[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  qo[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+int quantize_q8(const float* in, void* q, void* scales, long nblk, cudaStream_t st) {
+  if (nblk < 0 || (nblk > 0 && (!in || !q || !scales))) return record_status(ASPIDA_ERR_ARG);
+  if (((uintptr_t)in & 15) || ((uintptr_t)q & 15) || ((uintptr_t)scales & 1))
+    return record_status(ASPIDA_ERR_ARG);
+  if (nblk == 0) return 0;
+  const int threads = 128;
+  quantize_q8_kernel<<<(unsigned)((nblk + threads - 1) / threads), threads, 0, st>>>(
+      in, static_cast<int8_t*>(q), static_cast<__half*>(scales), nblk);
+  ASPIDA_CHECK_LAUNCH();
+  return 0;
+}
+
 }  // namespace aspida
+
+extern "C" int aspida_attn_decode_q8(const float* q, const float* gate, const void* const* K8,
+                                     const void* const* V8, const void* const* K_scales,
+                                     const void* const* V_scales, const int* pos,
+                                     const int* max_len, float* out, int B, int nq, int nkv,
+                                     int hd, float scale, int window, float softcap,
+                                     int max_kv_len, int chunk, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  return aspida::decode_q8(q, gate, K8, V8, K_scales, V_scales, pos, max_len, out, B, nq, nkv,
+                           hd, scale, window, softcap, max_kv_len, chunk, workspace,
+                           workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_quantize_q8(const float* in, void* q, void* scales, long long nblk,
+                                       void* stream) {
+  return aspida::quantize_q8(in, q, scales, (long)nblk, (cudaStream_t)stream);
+}
 
 extern "C" size_t aspida_attn_decode_workspace_size(int B, int nq, int nkv, int hd,
                                                     int max_kv_len, int chunk) {

@@ -165,6 +165,30 @@ int aspida_attn_decode_partial(const float* q, const void* const* K, const void*
                                int max_kv_len, int chunk, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Decode over Q8_0 KV caches: the storage of the reference's KVMODE 2
+ * (k_gqa_kv<..., 2>, gpu/fattn_kvhalf.cu:55-130; tile-load dequant at 88-92):
+ *   K8, V8          dev tables [B] of dev int8 caches [rows][nkv*hd]
+ *   K_scales, V_scales  dev tables [B] of dev fp16 scales [rows][nkv*hd/32],
+ *                   one per 32-value block along a row; value = int8 * scale
+ * Other arguments and the workspace as aspida_attn_decode. Caches 16-byte
+ * aligned. Supported: hd in {64, 128, 256} with nkv*hd >= 256 (a group of
+ * kv heads whose scales fill 16-byte units); else ASPIDA_ERR_UNSUPPORTED. */
+int aspida_attn_decode_q8(const float* q, const float* gate, const void* const* K8,
+                          const void* const* V8, const void* const* K_scales,
+                          const void* const* V_scales, const int* pos, const int* max_len,
+                          float* out, int B, int nq, int nkv, int hd, float scale, int window,
+                          float softcap, int max_kv_len, int chunk, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Q8_0 quantiser, the algorithm of k_to_q8 (gpu/fattn_kvhalf.cu:143-152):
+ * nblk blocks of 32 consecutive f32 values; scales[b] = fp16(max|v|/127),
+ * q = clamp(round-to-nearest-even(v * (1/d)), -127, 127), zeros for an
+ * all-zero block. Appending rows to a Q8_0 cache is this call on the rows'
+ * f32 values (nblk = rows*nkv*hd/32) with q/scales pointing at the rows.
+ * in and q 16-byte aligned. */
+int aspida_attn_quantize_q8(const float* in, void* q, void* scales, long long nblk,
+                            void* stream);
+
 /* Log-sum-exp merge of S partials (k_combine, gpu/fattn_sk.cu:84-97):
  *   m, l dev f32 [S][rows]; o dev f32 [S][rows][hd]; gate dev f32 [rows][hd]
  *   or NULL; out dev f32 [rows][hd] = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s. */

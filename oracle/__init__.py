@@ -161,3 +161,26 @@ def merge(m, l, o, gate=None):
     out = np.empty((rows, hd), np.float32)
     load().oracle_merge(_p(m), _p(l), _p(o), _p(g), _p(out), S, rows, hd)
     return out
+
+
+def quantize_q8(x):
+    """Q8_0 quantisation of k_to_q8 (gpu/fattn_kvhalf.cu:143-152), in numpy:
+    per 32-value block d = max|v| / 127 (f32 division), id = 1/d (0 for an
+    all-zero block), q = clamp(rint(v * id), -127, 127) (lrintf: nearest,
+    ties to even), scale = fp16(d). Returns (int8 q, fp16 scales)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    blocks = x.reshape(-1, 32)
+    amax = np.max(np.abs(blocks), axis=1)
+    d = (amax / np.float32(127)).astype(np.float32)
+    with np.errstate(divide="ignore"):
+        idv = np.where(d > 0, np.float32(1) / d, np.float32(0)).astype(np.float32)
+    qv = np.clip(np.rint(blocks * idv[:, None]), -127, 127).astype(np.int8)
+    return qv.reshape(x.shape), d.astype(np.float16).reshape(*x.shape[:-1], x.shape[-1] // 32)
+
+
+def dequantize_q8(q, scales):
+    """Values the reference's KVMODE 2 tile load computes
+    (gpu/fattn_kvhalf.cu:88-92): float(int8) * float(fp16 scale), in f32."""
+    q = np.asarray(q)
+    s = np.asarray(scales).astype(np.float32)
+    return (q.astype(np.float32).reshape(-1, 32) * s.reshape(-1, 1)).reshape(q.shape)

@@ -71,3 +71,39 @@ def chunk_inputs(c):
     K = r.standard_normal((ps + P, nkv * hd)).astype(np.float32)
     V = r.standard_normal((ps + P, nkv * hd)).astype(np.float32)
     return q, g, K, V
+
+
+# Q8_0 quantiser, reference kernel k_to_q8 (gpu/fattn_kvhalf.cu:143). Besides
+# random blocks the input holds an all-zero block, a one-value block, a block
+# of exact ties (max 127 so d = 1, values k + 0.5), negative extremes and a
+# large-magnitude block.
+Q8_QUANT_CASES = [
+    dict(name="q8quant_n4096", nblk=4096, seed=41),
+]
+
+# Gated causal GQA over a Q8_0 cache, reference kernel k_gqa_kv<2, hd/32, 2>
+# (gpu/fattn_kvhalf.cu:59), which quantises K/V with k_to_q8 first. P = 1 is
+# the decode shape (one query at position ps).
+Q8_GQA_CASES = [
+    dict(name="q8gqa_nq16_nkv2_hd256_P8_ps300", nq=16, nkv=2, hd=256, P=8, ps=300, seed=51),
+    dict(name="q8gqa_nq32_nkv8_hd128_P4_ps1000", nq=32, nkv=8, hd=128, P=4, ps=1000, seed=52),
+    dict(name="q8gqa_nq8_nkv2_hd128_P1_ps777", nq=8, nkv=2, hd=128, P=1, ps=777, seed=53),
+]
+
+
+def q8_quant_inputs(c):
+    r = np.random.RandomState(c["seed"])
+    x = (r.standard_normal((c["nblk"], 32)) * 2.0).astype(np.float32)
+    x[0] = 0.0
+    x[1] = 0.0
+    x[1, 7] = -3.25
+    x[2] = np.arange(32, dtype=np.float32) - 15.5   # ties once scaled
+    x[2, 0] = 127.0
+    x[3] = -np.abs(x[3])
+    x[4] *= 1000.0
+    x[5] = 1e-6 * r.standard_normal(32).astype(np.float32)
+    return x.reshape(-1)
+
+
+def q8_gqa_inputs(c):
+    return chunk_inputs(c)

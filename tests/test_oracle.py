@@ -54,6 +54,36 @@ def test_gated_chunk_matches_reference_kernel(oracle, c):
     np.testing.assert_allclose(got, ref, rtol=2e-5, atol=2e-6)
 
 
+def _npz(name):
+    p = os.path.join(GOLDEN, name + ".npz")
+    if not os.path.exists(p):
+        pytest.skip(f"golden fixture {name} not generated yet")
+    return np.load(p)
+
+
+@pytest.mark.parametrize("c", cases.Q8_QUANT_CASES, ids=lambda c: c["name"])
+def test_q8_quantiser_matches_reference_kernel(oracle, c):
+    """Bit-exact against k_to_q8 (gpu/fattn_kvhalf.cu:143) incl. zero, tie and
+    extreme blocks."""
+    x = cases.q8_quant_inputs(c)
+    ref = _npz(c["name"])
+    q, s = oracle.quantize_q8(x)
+    np.testing.assert_array_equal(q.reshape(-1), ref["q"])
+    np.testing.assert_array_equal(s.reshape(-1).view(np.uint16), ref["scales"].view(np.uint16))
+
+
+@pytest.mark.parametrize("c", cases.Q8_GQA_CASES, ids=lambda c: c["name"])
+def test_q8_gqa_matches_reference_kernel(oracle, c):
+    """The oracle's gated causal attention over the dequantised Q8_0 cache
+    against k_gqa_kv<2, hd/32, 2> (gpu/fattn_kvhalf.cu:59) on the same cache."""
+    q, g, K, V = cases.q8_gqa_inputs(c)
+    ref = _npz(c["name"])["out"].reshape(c["P"], -1)
+    Kd = oracle.dequantize_q8(*oracle.quantize_q8(K))
+    Vd = oracle.dequantize_q8(*oracle.quantize_q8(V))
+    got = oracle.prefill(q, Kd, Vd, c["ps"], c["nq"], c["nkv"], c["hd"], gate=g)
+    np.testing.assert_allclose(got, ref, rtol=2e-5, atol=2e-6)
+
+
 # ------------------------------------------------------- known-answer restated
 def test_closed_form_gqa_decode_known_answer(oracle):
     """ops.cu:131-153: nh8/nkv2/hd128/seq40 closed-form inputs, abs tol 1e-4,
