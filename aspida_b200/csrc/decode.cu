@@ -34,6 +34,7 @@
 //    dependent, so its launch overlaps the decode grid and only its merge
 //    work follows it.
 #include <algorithm>
+#include <type_traits>
 #include <cmath>
 
 #include "common.cuh"
@@ -170,7 +171,10 @@ struct Geometry {
   static constexpr int SLICE = HPC * HD * (Q8 ? 1 : 2);  // bytes of one row's group slice
   static constexpr int ROWB = SLICE + 16;                // padded smem row (conflict-free reads)
   static constexpr int SSL = Q8 ? HPC * HD / 16 : 0;     // bytes of one row's group scales
-  static constexpr int STAGE_BYTES = 2 * kKeys * ROWB + 2 * kKeys * SSL;
+  // Q8_0 rows sit in groups of 4 (one 4-row copy each) padded by 32 bytes
+  static constexpr int GRPB = 4 * SLICE + 32;
+  static constexpr int KVB = Q8 ? 4 * GRPB : kKeys * ROWB;  // bytes of one side's 16 rows
+  static constexpr int STAGE_BYTES = 2 * KVB + 2 * kKeys * SSL;
   static constexpr int STAGES_RAW = (kSmemBudget - (kMaxB + 1) * 4) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
   static constexpr int THREADS = (HPC + 1) * 32;
@@ -185,6 +189,24 @@ __device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t biased, uint32_t sel) 
   __half2 h = *reinterpret_cast<const __half2*>(&x);
   h = __hsub2(h, __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480)));
   return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Q8_0 stage layout: byte offset of stage row k (0..15) within one side.
+template <int SLICE>
+__device__ __forceinline__ int q8_row_off(int k) {
+  return (k >> 2) * (4 * SLICE + 32) + (k & 3) * SLICE;
+}
+// Q8_0 path: stage row held by MMA row m (S^T rows, P^T k index). Rows
+// m = 0..7 fall two per 4-row group, so each K read instruction has at most
+// 2-way bank conflicts; k indices 2t (and 2t+1, 2t+8, 2t+9), t = 0..3, fall
+// one per group, so each V read instruction is conflict-free.
+__device__ __forceinline__ int q8_sigma(int m) {
+  return 4 * ((m & 7) >> 1) + (m & 1) + 2 * (m >> 3);
+}
+
+// fp16 number i (0: low half) of a packed pair, as f32.
+__device__ __forceinline__ float half_of(uint32_t w, int i) {
+  return __half2float(__ushort_as_half((unsigned short)(i ? (w >> 16) : (w & 0xffffu))));
 }
 
 // Output dimension of accumulator element j of M tile mt. fp16 path: tile mt
@@ -239,6 +261,14 @@ decode_kernel(const DecodeParams p) {
   if (warp == HPC) {
     // ---------------- producer warp ----------------
     long fill = 0;
+    // this lane's cache base pointers, reloaded only when the sequence
+    // changes: a table read per stage would put a dependent global load on
+    // the producer's critical path every 16 keys
+    int cached_b = -1;
+    const unsigned char *kb = nullptr, *vb = nullptr;
+    [[maybe_unused]] const unsigned char *ksb = nullptr, *vsb = nullptr;
+    // Q8_0 with one head group per row: a stage's 16 rows are contiguous
+    [[maybe_unused]] const bool whole_row = HPC == p.nkv;
 #pragma unroll 1
     while (cur.valid) {
       const int slot = (int)(fill % STAGES);
@@ -251,31 +281,57 @@ decode_kernel(const DecodeParams p) {
       }
       if (lane == 0) mbar_arrive_expect_tx(&full[slot], Geo::STAGE_TX);
       __syncwarp();
-      const int which = lane >> 4;        // 0: K row, 1: V row
-      const int r = lane & 15;
-      const int key = min(cursor_key0(cur) + r, cur.hi - 1);  // past the end: repeat a valid row
+      if (cur.b != cached_b) {
+        cached_b = cur.b;
+        if constexpr (Q8) {
+          kb = reinterpret_cast<const unsigned char*>(p.K8[cur.b]);
+          vb = reinterpret_cast<const unsigned char*>(p.V8[cur.b]);
+          ksb = reinterpret_cast<const unsigned char*>(p.Ks[cur.b]);
+          vsb = reinterpret_cast<const unsigned char*>(p.Vs[cur.b]);
+        } else {
+          kb = reinterpret_cast<const unsigned char*>(p.block_table ? p.Kpool : p.K[cur.b]);
+          vb = reinterpret_cast<const unsigned char*>(p.block_table ? p.Vpool : p.V[cur.b]);
+        }
+      }
       unsigned char* dst = smem + slot * STAGE_BYTES;
+      const int key0 = cursor_key0(cur);
       if constexpr (Q8) {
-        const int8_t* base = which ? p.V8[cur.b] : p.K8[cur.b];
-        const __half* sbase = which ? p.Vs[cur.b] : p.Ks[cur.b];
-        bulk_g2s(dst + (which * kKeys + r) * ROWB,
-                 base + (long)key * p.nkv * HD + (long)cur.grp * HPC * HD, Geo::SLICE, &full[slot]);
-        bulk_g2s(dst + 2 * kKeys * ROWB + (which * kKeys + r) * Geo::SSL,
-                 sbase + (long)key * (p.nkv * HD / 32) + (long)cur.grp * (HPC * HD / 32), Geo::SSL,
-                 &full[slot]);
+        const long rowb = (long)p.nkv * HD, srowb = rowb / 16;  // bytes per cache / scale row
+        if (whole_row && key0 + kKeys <= cur.hi) {
+          // 4 copies of 4 rows per side + one copy of the 16 rows' scales per side
+          if (lane < 8) {
+            const int which = lane >> 2, gq = lane & 3;
+            bulk_g2s(dst + which * Geo::KVB + gq * Geo::GRPB,
+                     (which ? vb : kb) + (long)(key0 + 4 * gq) * rowb, 4 * Geo::SLICE, &full[slot]);
+          } else if (lane < 10) {
+            const int which = lane - 8;
+            bulk_g2s(dst + 2 * Geo::KVB + which * kKeys * Geo::SSL,
+                     (which ? vsb : ksb) + (long)key0 * srowb, kKeys * Geo::SSL, &full[slot]);
+          }
+        } else {
+          // row by row (segment end: rows past it repeat a valid row; or a
+          // head group that is part of a row)
+          const int which = lane >> 4, r = lane & 15;
+          const int key = min(key0 + r, cur.hi - 1);
+          bulk_g2s(dst + which * Geo::KVB + q8_row_off<Geo::SLICE>(r),
+                   (which ? vb : kb) + (long)key * rowb + (long)cur.grp * Geo::SLICE, Geo::SLICE,
+                   &full[slot]);
+          bulk_g2s(dst + 2 * Geo::KVB + (which * kKeys + r) * Geo::SSL,
+                   (which ? vsb : ksb) + (long)key * srowb + (long)cur.grp * Geo::SSL, Geo::SSL,
+                   &full[slot]);
+        }
       } else {
-        const __half* base;
-        long row;
+        const int which = lane >> 4;        // 0: K row, 1: V row
+        const int r = lane & 15;
+        const int key = min(key0 + r, cur.hi - 1);  // past the end: repeat a valid row
+        long row = key;
         if (p.block_table) {            // paged: key -> (block id, row in block)
-          base = which ? p.Vpool : p.Kpool;
           const int blk = p.block_table[(long)cur.b * p.max_blocks + key / p.block_size];
           row = (long)blk * p.block_size + key % p.block_size;
-        } else {
-          base = which ? p.V[cur.b] : p.K[cur.b];
-          row = key;
         }
-        const __half* src = base + row * p.nkv * HD + (long)cur.grp * HPC * HD;
-        bulk_g2s(dst + (which * kKeys + r) * ROWB, src, Geo::SLICE, &full[slot]);
+        bulk_g2s(dst + (which * kKeys + r) * ROWB,
+                 (which ? vb : kb) + 2 * (row * p.nkv * HD + (long)cur.grp * HPC * HD),
+                 Geo::SLICE, &full[slot]);
       }
       ++fill;
       ++cur.u;
@@ -294,6 +350,18 @@ decode_kernel(const DecodeParams p) {
   long consumed = 0;
   const int krow = (lane & 7) + ((lane >> 3) & 1) * 8, kcol = (lane >> 4) * 8;
   const int vrow = (lane & 7) + (lane >> 4) * 8, vcol = ((lane >> 3) & 1) * 8;
+  // Q8_0: stage rows of MMA rows g and g+8, their K byte offsets, and the V
+  // byte offsets of k indices 2t, 2t+1, 2t+8, 2t+9
+  [[maybe_unused]] const int q_r0 = q8_sigma(g), q_r1 = q8_sigma(g + 8);
+  [[maybe_unused]] const int q_k0 = q8_row_off<Geo::SLICE>(q_r0), q_k1 = q8_row_off<Geo::SLICE>(q_r1);
+  [[maybe_unused]] int q_v[4];
+  {
+    const int t = lane & 3;
+    q_v[0] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t));
+    q_v[1] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t + 1));
+    q_v[2] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t + 8));
+    q_v[3] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t + 9));
+  }
 
 #pragma unroll 1
   while (cur.valid) {
@@ -330,133 +398,194 @@ decode_kernel(const DecodeParams p) {
       m_run[0] = m_run[1] = -INFINITY;
       l_run[0] = l_run[1] = 0.f;
     }
-    const int slot = (int)(consumed % STAGES);
-    if (!mbar_wait_bounded(&full[slot], (uint32_t)((consumed / STAGES) & 1))) {
-      if (lane == 0 && p.status) { atomicExch(&p.status->code, kDevTimeoutMbar); p.status->where = 11; }
-      return;
-    }
-    const unsigned char* st = smem + slot * STAGE_BYTES + h * HD * (Q8 ? 1 : 2);
-    const uint32_t kbase = smem_u32(st), vbase = smem_u32(st + kKeys * ROWB);
-    [[maybe_unused]] const __half* ksc = nullptr;
-    [[maybe_unused]] const __half* vsc = nullptr;
-
-    float s4[4] = {0.f, 0.f, 0.f, 0.f};
-    if constexpr (Q8) {
-      // per 32-dim block: integer K (exact in fp16) times Q, then the block's
-      // per-key scale in f32
-      const unsigned char* sc = smem + slot * STAGE_BYTES + 2 * kKeys * ROWB + h * (HD / 16);
-      ksc = reinterpret_cast<const __half*>(sc);
-      vsc = reinterpret_cast<const __half*>(sc + kKeys * Geo::SSL);
-      const int t = lane & 3;
+    // A pass handles NU consecutive units of a piece under one softmax
+    // update. Passes take one unit: two per pass (one max over 32 keys,
+    // interleaved MMA chains) measured slower on B200 for both cache types.
+    const long piece_end = min(cur.seg_u1, u_end);
+    constexpr int nu = 1;
+    bool ok = true;
+    auto pass = [&](auto nu_c) {
+      constexpr int NU = decltype(nu_c)::value;
+      int slot[NU];
 #pragma unroll
-      for (int blk = 0; blk < HD / 32; ++blk) {
-        float sb[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int kk = 0; kk < 2; ++kk) {
-          const int kt = 2 * blk + kk;
-          const uint32_t w0 = lds_u32(kbase + g * ROWB + kt * 16 + 4 * t) ^ 0x80808080u;
-          const uint32_t w1 = lds_u32(kbase + (g + 8) * ROWB + kt * 16 + 4 * t) ^ 0x80808080u;
-          uint32_t a[4];
-          a[0] = i8pair_to_h2(w0, 0x4140);
-          a[1] = i8pair_to_h2(w1, 0x4140);
-          a[2] = i8pair_to_h2(w0, 0x4342);
-          a[3] = i8pair_to_h2(w1, 0x4342);
-          mma_16816(sb, a, qlo[kt][0], qlo[kt][1]);
-          mma_16816(sb, a, qhi[kt][0], qhi[kt][1]);
+      for (int i = 0; i < NU; ++i) {
+        slot[i] = (int)((consumed + i) % STAGES);
+        if (!mbar_wait_bounded(&full[slot[i]], (uint32_t)(((consumed + i) / STAGES) & 1))) {
+          if (lane == 0 && p.status) { atomicExch(&p.status->code, kDevTimeoutMbar); p.status->where = 11; }
+          ok = false;
+          return;
         }
-        const float c0 = __half2float(ksc[g * (Geo::SSL / 2) + blk]);
-        const float c1 = __half2float(ksc[(g + 8) * (Geo::SSL / 2) + blk]);
-        s4[0] = fmaf(c0, sb[0], s4[0]);
-        s4[1] = fmaf(c0, sb[1], s4[1]);
-        s4[2] = fmaf(c1, sb[2], s4[2]);
-        s4[3] = fmaf(c1, sb[3], s4[3]);
       }
-    } else {
-      // S^T = K (Q_hi + Q_lo)^T for 16 keys x 8 query columns
+      uint32_t kbase[NU], vbase[NU];
+      // Q8_0: this head's block scales of key rows g and g+8 (K, then V), as
+      // packed fp16 pairs, HD/64 words per row
+      [[maybe_unused]] uint32_t kscw[NU][2][HD / 64], vscw[NU][2][HD / 64];
+      float s4[NU][4];
+#pragma unroll
+      for (int i = 0; i < NU; ++i) {
+        const unsigned char* st = smem + slot[i] * STAGE_BYTES + h * HD * (Q8 ? 1 : 2);
+        kbase[i] = smem_u32(st);
+        vbase[i] = smem_u32(st + Geo::KVB);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) s4[i][j] = 0.f;
+      }
+      if constexpr (Q8) {
+        const int t = lane & 3;
+#pragma unroll
+        for (int i = 0; i < NU; ++i) {
+          const uint32_t sc = smem_u32(smem + slot[i] * STAGE_BYTES + 2 * Geo::KVB) + h * (HD / 16);
+#pragma unroll
+          for (int w = 0; w < HD / 64; ++w) {
+            kscw[i][0][w] = lds_u32(sc + q_r0 * Geo::SSL + 4 * w);
+            kscw[i][1][w] = lds_u32(sc + q_r1 * Geo::SSL + 4 * w);
+            vscw[i][0][w] = lds_u32(sc + (kKeys + q_r0) * Geo::SSL + 4 * w);
+            vscw[i][1][w] = lds_u32(sc + (kKeys + q_r1) * Geo::SSL + 4 * w);
+          }
+        }
+        // per 32-dim block: integer K (exact in fp16) times Q, then the
+        // block's per-key scale in f32
+#pragma unroll
+        for (int blk = 0; blk < HD / 32; ++blk) {
+#pragma unroll
+          for (int i = 0; i < NU; ++i) {
+            float sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int kk = 0; kk < 2; ++kk) {
+              const int kt = 2 * blk + kk;
+              const uint32_t w0 = lds_u32(kbase[i] + q_k0 + kt * 16 + 4 * t) ^ 0x80808080u;
+              const uint32_t w1 = lds_u32(kbase[i] + q_k1 + kt * 16 + 4 * t) ^ 0x80808080u;
+              uint32_t a[4];
+              a[0] = i8pair_to_h2(w0, 0x4140);
+              a[1] = i8pair_to_h2(w1, 0x4140);
+              a[2] = i8pair_to_h2(w0, 0x4342);
+              a[3] = i8pair_to_h2(w1, 0x4342);
+              mma_16816(sb, a, qlo[kt][0], qlo[kt][1]);
+              mma_16816(sb, a, qhi[kt][0], qhi[kt][1]);
+            }
+            const float c0 = half_of(kscw[i][0][blk >> 1], blk & 1);
+            const float c1 = half_of(kscw[i][1][blk >> 1], blk & 1);
+            s4[i][0] = fmaf(c0, sb[0], s4[i][0]);
+            s4[i][1] = fmaf(c0, sb[1], s4[i][1]);
+            s4[i][2] = fmaf(c1, sb[2], s4[i][2]);
+            s4[i][3] = fmaf(c1, sb[3], s4[i][3]);
+          }
+        }
+      } else {
+        // S^T = K (Q_hi + Q_lo)^T for 16 keys x 8 query columns
+#pragma unroll
+        for (int kt = 0; kt < KT; ++kt) {
+#pragma unroll
+          for (int i = 0; i < NU; ++i) {
+            uint32_t a[4];
+            ldmatrix_x4(a[0], a[1], a[2], a[3], kbase[i] + krow * ROWB + (kt * 16 + kcol) * 2);
+            mma_16816(s4[i], a, qlo[kt][0], qlo[kt][1]);
+            mma_16816(s4[i], a, qhi[kt][0], qhi[kt][1]);
+          }
+        }
+      }
+      // scale (+ softcap), mask keys past the segment's end
+      const int key0 = cursor_key0(cur);
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < NU; ++i) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float x = s4[i][j];
+          if (p.softcap > 0.f) x = p.softcap * tanhf(x * (p.scale_log2 / kLog2e) / p.softcap) * kLog2e;
+          else x *= p.scale_log2;
+          const int r = Q8 ? ((j >> 1) ? q_r1 : q_r0) : g + (j >> 1) * 8;  // stage row
+          s4[i][j] = key0 + i * kKeys + r < cur.hi ? x : -INFINITY;
+        }
+        mx0 = fmaxf(mx0, fmaxf(s4[i][0], s4[i][2]));
+        mx1 = fmaxf(mx1, fmaxf(s4[i][1], s4[i][3]));
+      }
+      // online softmax per query column (qc, qc + 1)
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
+      const float c0 = fast_exp2(m_run[0] - mn0), c1 = fast_exp2(m_run[1] - mn1);
+      m_run[0] = mn0;
+      m_run[1] = mn1;
+      float pr[NU][4];
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NU; ++i) {
+        pr[i][0] = fast_exp2(s4[i][0] - mn0);
+        pr[i][1] = fast_exp2(s4[i][1] - mn1);
+        pr[i][2] = fast_exp2(s4[i][2] - mn0);
+        pr[i][3] = fast_exp2(s4[i][3] - mn1);
+        ls0 += pr[i][0] + pr[i][2];
+        ls1 += pr[i][1] + pr[i][3];
+      }
+      l_run[0] = l_run[0] * c0 + ls0;
+      l_run[1] = l_run[1] * c1 + ls1;
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
-        uint32_t a[4];
-        ldmatrix_x4(a[0], a[1], a[2], a[3], kbase + krow * ROWB + (kt * 16 + kcol) * 2);
-        mma_16816(s4, a, qlo[kt][0], qlo[kt][1]);
-        mma_16816(s4, a, qhi[kt][0], qhi[kt][1]);
+        oacc[kt][0] *= c0; oacc[kt][1] *= c1;
+        oacc[kt][2] *= c0; oacc[kt][3] *= c1;
       }
-    }
-    // scale (+ softcap), mask keys past the segment's end
-    const int key0 = cursor_key0(cur);
+      if constexpr (Q8) {
+        // Per 32-dim block: P times the block's per-key V scale (and
+        // kVScale), transposed into the B operand; V^T as exact integers
+        // from four 4-byte reads (the stage rows of k indices 2t, 2t+1,
+        // 2t+8, 2t+9, at dims 4g..4g+3).
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float x = s4[j];
-      if (p.softcap > 0.f) x = p.softcap * tanhf(x * (p.scale_log2 / kLog2e) / p.softcap) * kLog2e;
-      else x *= p.scale_log2;
-      s4[j] = key0 + g + (j >> 1) * 8 < cur.hi ? x : -INFINITY;
-    }
-    // online softmax per query column (qc, qc + 1)
-    float mx0 = fmaxf(s4[0], s4[2]), mx1 = fmaxf(s4[1], s4[3]);
+        for (int blk = 0; blk < HD / 32; ++blk) {
 #pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-    }
-    const float mn0 = fmaxf(m_run[0], mx0), mn1 = fmaxf(m_run[1], mx1);
-    const float c0 = fast_exp2(m_run[0] - mn0), c1 = fast_exp2(m_run[1] - mn1);
-    m_run[0] = mn0;
-    m_run[1] = mn1;
-    const float p0 = fast_exp2(s4[0] - mn0), p1 = fast_exp2(s4[1] - mn1);
-    const float p2 = fast_exp2(s4[2] - mn0), p3 = fast_exp2(s4[3] - mn1);
-    l_run[0] = l_run[0] * c0 + (p0 + p2);
-    l_run[1] = l_run[1] * c1 + (p1 + p3);
+          for (int i = 0; i < NU; ++i) {
+            const float v0 = half_of(vscw[i][0][blk >> 1], blk & 1) * kVScale;
+            const float v1 = half_of(vscw[i][1][blk >> 1], blk & 1) * kVScale;
+            const uint32_t b0 = movmatrix_trans(pack_half2(pr[i][0] * v0, pr[i][1] * v0));
+            const uint32_t b1 = movmatrix_trans(pack_half2(pr[i][2] * v1, pr[i][3] * v1));
+            const uint32_t col = vbase[i] + blk * 32 + 4 * g;
+            const uint32_t x0 = lds_u32(col + q_v[0]) ^ 0x80808080u;
+            const uint32_t x1 = lds_u32(col + q_v[1]) ^ 0x80808080u;
+            const uint32_t x2 = lds_u32(col + q_v[2]) ^ 0x80808080u;
+            const uint32_t x3 = lds_u32(col + q_v[3]) ^ 0x80808080u;
+            // byte-interleave rows: lo = dims 0,1 of both keys, hi = dims 2,3
+            const uint32_t l01 = __byte_perm(x0, x1, 0x5140), h01 = __byte_perm(x0, x1, 0x7362);
+            const uint32_t l23 = __byte_perm(x2, x3, 0x5140), h23 = __byte_perm(x2, x3, 0x7362);
+            uint32_t a[4];
+            a[0] = i8pair_to_h2(l01, 0x4140);  // dim 4g   (tile 2blk row g),   keys 2t, 2t+1
+            a[1] = i8pair_to_h2(l01, 0x4342);  // dim 4g+1 (tile 2blk row g+8)
+            a[2] = i8pair_to_h2(l23, 0x4140);  // dim 4g,   keys 2t+8, 2t+9
+            a[3] = i8pair_to_h2(l23, 0x4342);
+            mma_16816(oacc[2 * blk], a, b0, b1);
+            a[0] = i8pair_to_h2(h01, 0x4140);  // dims 4g+2, 4g+3 (tile 2blk+1)
+            a[1] = i8pair_to_h2(h01, 0x4342);
+            a[2] = i8pair_to_h2(h23, 0x4140);
+            a[3] = i8pair_to_h2(h23, 0x4342);
+            mma_16816(oacc[2 * blk + 1], a, b0, b1);
+          }
+        }
+      } else {
+        // P^T operand via in-register transpose, then O^T += V^T P^T
 #pragma unroll
-    for (int kt = 0; kt < KT; ++kt) {
-      oacc[kt][0] *= c0; oacc[kt][1] *= c1;
-      oacc[kt][2] *= c0; oacc[kt][3] *= c1;
-    }
-    if constexpr (Q8) {
-      // Per 32-dim block: P times the block's per-key V scale (and kVScale),
-      // transposed into the B operand; V^T as exact integers from four
-      // 4-byte reads (keys 2t, 2t+1, 2t+8, 2t+9 at dims 4g..4g+3).
-      const int t = lane & 3;
+        for (int i = 0; i < NU; ++i) {
+          const uint32_t b0 = movmatrix_trans(pack_half2(pr[i][0], pr[i][1]));
+          const uint32_t b1 = movmatrix_trans(pack_half2(pr[i][2], pr[i][3]));
 #pragma unroll
-      for (int blk = 0; blk < HD / 32; ++blk) {
-        const float v0 = __half2float(vsc[g * (Geo::SSL / 2) + blk]) * kVScale;
-        const float v1 = __half2float(vsc[(g + 8) * (Geo::SSL / 2) + blk]) * kVScale;
-        const uint32_t b0 = movmatrix_trans(pack_half2(p0 * v0, p1 * v0));
-        const uint32_t b1 = movmatrix_trans(pack_half2(p2 * v1, p3 * v1));
-        const uint32_t col = vbase + blk * 32 + 4 * g;
-        const uint32_t x0 = lds_u32(col + (2 * t) * ROWB) ^ 0x80808080u;
-        const uint32_t x1 = lds_u32(col + (2 * t + 1) * ROWB) ^ 0x80808080u;
-        const uint32_t x2 = lds_u32(col + (2 * t + 8) * ROWB) ^ 0x80808080u;
-        const uint32_t x3 = lds_u32(col + (2 * t + 9) * ROWB) ^ 0x80808080u;
-        // byte-interleave rows: lo = dims 0,1 of both keys, hi = dims 2,3
-        const uint32_t l01 = __byte_perm(x0, x1, 0x5140), h01 = __byte_perm(x0, x1, 0x7362);
-        const uint32_t l23 = __byte_perm(x2, x3, 0x5140), h23 = __byte_perm(x2, x3, 0x7362);
-        uint32_t a[4];
-        a[0] = i8pair_to_h2(l01, 0x4140);  // dim 4g   (tile 2blk row g),   keys 2t, 2t+1
-        a[1] = i8pair_to_h2(l01, 0x4342);  // dim 4g+1 (tile 2blk row g+8)
-        a[2] = i8pair_to_h2(l23, 0x4140);  // dim 4g,   keys 2t+8, 2t+9
-        a[3] = i8pair_to_h2(l23, 0x4342);
-        mma_16816(oacc[2 * blk], a, b0, b1);
-        a[0] = i8pair_to_h2(h01, 0x4140);  // dims 4g+2, 4g+3 (tile 2blk+1)
-        a[1] = i8pair_to_h2(h01, 0x4342);
-        a[2] = i8pair_to_h2(h23, 0x4140);
-        a[3] = i8pair_to_h2(h23, 0x4342);
-        mma_16816(oacc[2 * blk + 1], a, b0, b1);
+          for (int mt = 0; mt < KT; ++mt) {
+            uint32_t a[4];
+            ldmatrix_x4_trans(a[0], a[1], a[2], a[3], vbase[i] + vrow * ROWB + (mt * 16 + vcol) * 2);
+            mma_16816(oacc[mt], a, b0, b1);
+          }
+        }
       }
-    } else {
-      // P^T operand via in-register transpose, then O^T += V^T P^T
-      const uint32_t b0 = movmatrix_trans(pack_half2(p0, p1));
-      const uint32_t b1 = movmatrix_trans(pack_half2(p2, p3));
+      __syncwarp();
+      if (lane == 0) {
 #pragma unroll
-      for (int mt = 0; mt < KT; ++mt) {
-        uint32_t a[4];
-        ldmatrix_x4_trans(a[0], a[1], a[2], a[3], vbase + vrow * ROWB + (mt * 16 + vcol) * 2);
-        mma_16816(oacc[mt], a, b0, b1);
+        for (int i = 0; i < NU; ++i) mbar_arrive(&empty[slot[i]]);   // slots may be refilled
       }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);   // slot may be refilled
-    ++consumed;
+    };
+    pass(std::integral_constant<int, nu>{});
+    if (!ok) return;
+    consumed += nu;
 
-    if ((cur.u + 1 == cur.seg_u1) || (cur.u + 1 == u_end)) {
+    if (cur.u + nu == piece_end) {
       // piece done: reduce l across the lanes that share a query column
       float l0 = l_run[0], l1 = l_run[1];
 #pragma unroll
@@ -522,7 +651,7 @@ decode_kernel(const DecodeParams p) {
         }
       }
     }
-    ++cur.u;
+    cur.u += nu;
     cursor_seek(p, pref, cur);
   }
 }

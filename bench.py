@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only warm-up + timed steps of one leg, no clock soak, e2e or CPU")
-    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long"], default="decode")
+    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long", "q8"], default="decode")
     return ap.parse_args()
 
 
@@ -223,6 +223,44 @@ def long_leg(ab, torch, dev, rank, world, steps, warmup, stream, dist):
     return e0.elapsed_time(e1) / steps, n * nkv * hd * 2 * 2
 
 
+def q8_leg(ab, torch, dev, lens, steps, warmup, stream, seed):
+    """Config-2 batch on Q8_0 caches (int8 + fp16 scale per 32 values, the
+    reference's KVMODE 2 storage), quantised on the device from seeded N(0,1)
+    f32. Returns (ms per step, algorithmic bytes per step)."""
+    g = torch.Generator(device=dev).manual_seed(seed)
+    kvd = NKV * HD
+    K8, V8, Ks, Vs = [], [], [], []
+    for L in lens:
+        for dst8, dsts in ((K8, Ks), (V8, Vs)):
+            x = torch.randn(L, kvd, generator=g, device=dev)
+            a, s = ab.quantize_q8(x)
+            dst8.append(a)
+            dsts.append(s)
+            del x
+    tabs = [ab.ptr_table(t, dev) for t in (K8, V8, Ks, Vs)]
+    q = torch.randn(len(lens), NQ * HD, generator=g, device=dev)
+    pos = torch.tensor([L - 1 for L in lens], dtype=torch.int32, device=dev)
+    out = torch.empty(len(lens), NQ * HD, device=dev)
+    ws = ab.Workspace()
+    maxkv = max(lens)
+
+    def step():
+        ab.decode_q8(q, *tabs, pos, NQ, NKV, HD, max_kv_len=maxkv, out=out, workspace=ws,
+                     stream=stream)
+
+    for _ in range(max(3, warmup)):
+        step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    nbytes = sum(lens) * kvd * 2 * (1 + 2 / 32) + len(lens) * NQ * HD * 8
+    return e0.elapsed_time(e1) / steps, nbytes
+
+
 def prefill_cpu_sample(q, K, V, seconds=8.0):
     """CPU oracle on the last rows of one config-3 sequence (causal flops of
     those rows / time), all host cores."""
@@ -340,6 +378,10 @@ def main():
         if args.profile_leg == "decode":
             for _ in range(args.steps):
                 step()
+        elif args.profile_leg == "q8":
+            for c in caches:
+                c.free()
+            q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4000 + rank)
         elif args.profile_leg == "prefill":
             for c in caches:
                 c.free()
@@ -407,20 +449,25 @@ def main():
         raise RuntimeError("device status after prefill")
     l_ms, l_bytes = long_leg(ab, torch, dev, rank, world, max(10, min(args.steps, 100)),
                              args.warmup, stream, dist)
+    torch.cuda.empty_cache()
+    q_ms, q_bytes = q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4000 + rank)
+    if ab.device_status() != 0:
+        raise RuntimeError("device status after q8 decode")
 
     nbytes = algo_bytes(lens)
-    stats = torch.tensor([ms, ms_e2e, p_ms, l_ms, float(nbytes), float(p_flops), float(l_bytes)],
-                         dtype=torch.float64, device=dev)
+    stats = torch.tensor([ms, ms_e2e, p_ms, l_ms, q_ms, float(nbytes), float(p_flops),
+                          float(l_bytes), float(q_bytes)], dtype=torch.float64, device=dev)
     if dist:
-        mx = stats[:4].clone()
+        mx = stats[:5].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = stats[4:].clone()
+        tot = stats[5:].clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms_max, ms_e2e_max, p_ms_max, l_ms_max = (float(x) for x in mx)
-        bytes_all, flops_all, l_bytes_all = (float(x) for x in tot)
+        ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max = (float(x) for x in mx)
+        bytes_all, flops_all, l_bytes_all, q_bytes_all = (float(x) for x in tot)
     else:
-        ms_max, ms_e2e_max, p_ms_max, l_ms_max = ms, ms_e2e, p_ms, l_ms
-        bytes_all, flops_all, l_bytes_all = float(nbytes), float(p_flops), float(l_bytes)
+        ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max = ms, ms_e2e, p_ms, l_ms, q_ms
+        bytes_all, flops_all, l_bytes_all, q_bytes_all = (float(nbytes), float(p_flops),
+                                                          float(l_bytes), float(q_bytes))
 
     if rank == 0:
         hbm, src = peaks()
@@ -476,6 +523,18 @@ def main():
                 "frac_of_hbm_x_gpus": round(l_bytes_all / (l_ms_max * 1e-3) / 1e9
                                             / (peaks()[0] * world), 4),
             },
+        }
+        line["decode_q8"] = {
+            "metric": "decode attn KV GB/s over Q8_0 caches (cfg2 lengths and heads, int8 + "
+                      "fp16 scale per 32 values)",
+            "value": round(q_bytes_all / (q_ms_max * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(q_ms_max, 5),
+            "speedup_vs_fp16_kv": round(ms_max / q_ms_max, 3),
+            "bytes_per_step_per_gpu": int(q_bytes),
+            "roofline": {"bound": "hbm", "achieved": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
+                         "peak": peaks()[0], "unit": "GB/s",
+                         "frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks()[0], 4)},
+            "gpu_launches": args.steps * 2,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(lens, args.cpu_seconds,
