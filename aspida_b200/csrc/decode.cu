@@ -169,11 +169,15 @@ __device__ __forceinline__ int cursor_key0(const Cursor& c) {
 template <int HD, int HPC, bool Q8>
 struct Geometry {
   static constexpr int SLICE = HPC * HD * (Q8 ? 1 : 2);  // bytes of one row's group slice
-  static constexpr int ROWB = SLICE + 16;                // padded smem row (conflict-free reads)
   static constexpr int SSL = Q8 ? HPC * HD / 16 : 0;     // bytes of one row's group scales
-  // Q8_0 rows sit in groups of 4 (one 4-row copy each) padded by 32 bytes
-  static constexpr int GRPB = 4 * SLICE + 32;
-  static constexpr int KVB = Q8 ? 4 * GRPB : kKeys * ROWB;  // bytes of one side's 16 rows
+  // A side's 16 stage rows sit in groups of RG consecutive rows padded by
+  // PADG bytes. Q8_0: 4-row groups, one bulk copy each when the head group
+  // is a whole cache row (the copy engine, not DRAM, bounds 1 KB row copies).
+  // fp16: single rows (2 KB copies; 2-row copies measured no faster on the
+  // batched shape and 4% slower on one long sequence).
+  static constexpr int RG = Q8 ? 4 : 1, PADG = Q8 ? 32 : 16;
+  static constexpr int GRPB = RG * SLICE + PADG;
+  static constexpr int KVB = (kKeys / RG) * GRPB;        // bytes of one side's 16 rows
   static constexpr int STAGE_BYTES = 2 * KVB + 2 * kKeys * SSL;
   static constexpr int STAGES_RAW = (kSmemBudget - (kMaxB + 1) * 4) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : (STAGES_RAW < 2 ? 2 : STAGES_RAW);
@@ -191,17 +195,23 @@ __device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t biased, uint32_t sel) 
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Q8_0 stage layout: byte offset of stage row k (0..15) within one side.
-template <int SLICE>
-__device__ __forceinline__ int q8_row_off(int k) {
-  return (k >> 2) * (4 * SLICE + 32) + (k & 3) * SLICE;
+// Byte offset of stage row k (0..15) within one side of a stage.
+template <class Geo>
+__device__ __forceinline__ int row_off(int k) {
+  return (k / Geo::RG) * Geo::GRPB + (k % Geo::RG) * Geo::SLICE;
 }
-// Q8_0 path: stage row held by MMA row m (S^T rows, P^T k index). Rows
-// m = 0..7 fall two per 4-row group, so each K read instruction has at most
-// 2-way bank conflicts; k indices 2t (and 2t+1, 2t+8, 2t+9), t = 0..3, fall
-// one per group, so each V read instruction is conflict-free.
-__device__ __forceinline__ int q8_sigma(int m) {
-  return 4 * ((m & 7) >> 1) + (m & 1) + 2 * (m >> 3);
+// Stage row held by MMA row m (the S^T row, and the k index of P^T / V^T).
+// A slice is a multiple of 128 bytes, so rows of one group share banks and
+// only the group padding separates them.
+//  fp16 (1-row groups, 16-byte pad): identity; every 8-row ldmatrix phase
+//    reads eight distinct 16-byte bank groups.
+//  Q8_0 (4-row groups, 32-byte pad): MMA rows 0..7 fall two per group (K
+//    reads at most 2-way conflicted); k indices 2t (and 2t+1, 2t+8, 2t+9),
+//    t = 0..3, fall one per group (V reads conflict-free).
+template <bool Q8>
+__device__ __forceinline__ int stage_row(int m) {
+  if constexpr (Q8) return 4 * ((m & 7) >> 1) + (m & 1) + 2 * (m >> 3);
+  else return m;
 }
 
 // fp16 number i (0: low half) of a packed pair, as f32.
@@ -223,7 +233,7 @@ template <int HD, int HPC, bool Q8>
 __global__ void __launch_bounds__(Geometry<HD, HPC, Q8>::THREADS, 1)
 decode_kernel(const DecodeParams p) {
   using Geo = Geometry<HD, HPC, Q8>;
-  constexpr int ROWB = Geo::ROWB, STAGE_BYTES = Geo::STAGE_BYTES, STAGES = Geo::STAGES;
+  constexpr int STAGE_BYTES = Geo::STAGE_BYTES, STAGES = Geo::STAGES;
   constexpr int KT = HD / 16;   // 16-dim steps
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) uint64_t full[STAGES], empty[STAGES];
@@ -267,7 +277,7 @@ decode_kernel(const DecodeParams p) {
     int cached_b = -1;
     const unsigned char *kb = nullptr, *vb = nullptr;
     [[maybe_unused]] const unsigned char *ksb = nullptr, *vsb = nullptr;
-    // Q8_0 with one head group per row: a stage's 16 rows are contiguous
+    // one head group per row: a stage's 16 rows are contiguous
     [[maybe_unused]] const bool whole_row = HPC == p.nkv;
 #pragma unroll 1
     while (cur.valid) {
@@ -313,7 +323,7 @@ decode_kernel(const DecodeParams p) {
           // head group that is part of a row)
           const int which = lane >> 4, r = lane & 15;
           const int key = min(key0 + r, cur.hi - 1);
-          bulk_g2s(dst + which * Geo::KVB + q8_row_off<Geo::SLICE>(r),
+          bulk_g2s(dst + which * Geo::KVB + row_off<Geo>(r),
                    (which ? vb : kb) + (long)key * rowb + (long)cur.grp * Geo::SLICE, Geo::SLICE,
                    &full[slot]);
           bulk_g2s(dst + 2 * Geo::KVB + (which * kKeys + r) * Geo::SSL,
@@ -321,6 +331,7 @@ decode_kernel(const DecodeParams p) {
                    &full[slot]);
         }
       } else {
+        const long rowb = 2L * p.nkv * HD;  // bytes per cache row
         const int which = lane >> 4;        // 0: K row, 1: V row
         const int r = lane & 15;
         const int key = min(key0 + r, cur.hi - 1);  // past the end: repeat a valid row
@@ -329,9 +340,9 @@ decode_kernel(const DecodeParams p) {
           const int blk = p.block_table[(long)cur.b * p.max_blocks + key / p.block_size];
           row = (long)blk * p.block_size + key % p.block_size;
         }
-        bulk_g2s(dst + (which * kKeys + r) * ROWB,
-                 (which ? vb : kb) + 2 * (row * p.nkv * HD + (long)cur.grp * HPC * HD),
-                 Geo::SLICE, &full[slot]);
+        bulk_g2s(dst + which * Geo::KVB + row_off<Geo>(r),
+                 (which ? vb : kb) + row * rowb + (long)cur.grp * Geo::SLICE, Geo::SLICE,
+                 &full[slot]);
       }
       ++fill;
       ++cur.u;
@@ -348,19 +359,23 @@ decode_kernel(const DecodeParams p) {
   float oacc[KT][4];
   float m_run[2], l_run[2];
   long consumed = 0;
-  const int krow = (lane & 7) + ((lane >> 3) & 1) * 8, kcol = (lane >> 4) * 8;
-  const int vrow = (lane & 7) + (lane >> 4) * 8, vcol = ((lane >> 3) & 1) * 8;
-  // Q8_0: stage rows of MMA rows g and g+8, their K byte offsets, and the V
-  // byte offsets of k indices 2t, 2t+1, 2t+8, 2t+9
-  [[maybe_unused]] const int q_r0 = q8_sigma(g), q_r1 = q8_sigma(g + 8);
-  [[maybe_unused]] const int q_k0 = q8_row_off<Geo::SLICE>(q_r0), q_k1 = q8_row_off<Geo::SLICE>(q_r1);
+  // fp16: ldmatrix row addresses of K (MMA row krow) and V^T (k index vrow)
+  const int kcol = (lane >> 4) * 8, vcol = ((lane >> 3) & 1) * 8;
+  [[maybe_unused]] const int krow_off =
+      row_off<Geo>(stage_row<Q8>((lane & 7) + ((lane >> 3) & 1) * 8));
+  [[maybe_unused]] const int vrow_off = row_off<Geo>(stage_row<Q8>((lane & 7) + (lane >> 4) * 8));
+  // stage rows of MMA rows g and g+8 (masking, Q8_0 scales)
+  const int q_r0 = stage_row<Q8>(g), q_r1 = stage_row<Q8>(g + 8);
+  // Q8_0: K byte offsets of those rows, V byte offsets of k indices 2t,
+  // 2t+1, 2t+8, 2t+9
+  [[maybe_unused]] const int q_k0 = row_off<Geo>(q_r0), q_k1 = row_off<Geo>(q_r1);
   [[maybe_unused]] int q_v[4];
   {
     const int t = lane & 3;
-    q_v[0] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t));
-    q_v[1] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t + 1));
-    q_v[2] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t + 8));
-    q_v[3] = q8_row_off<Geo::SLICE>(q8_sigma(2 * t + 9));
+    q_v[0] = row_off<Geo>(stage_row<Q8>(2 * t));
+    q_v[1] = row_off<Geo>(stage_row<Q8>(2 * t + 1));
+    q_v[2] = row_off<Geo>(stage_row<Q8>(2 * t + 8));
+    q_v[3] = row_off<Geo>(stage_row<Q8>(2 * t + 9));
   }
 
 #pragma unroll 1
@@ -477,7 +492,7 @@ decode_kernel(const DecodeParams p) {
 #pragma unroll
           for (int i = 0; i < NU; ++i) {
             uint32_t a[4];
-            ldmatrix_x4(a[0], a[1], a[2], a[3], kbase[i] + krow * ROWB + (kt * 16 + kcol) * 2);
+            ldmatrix_x4(a[0], a[1], a[2], a[3], kbase[i] + krow_off + (kt * 16 + kcol) * 2);
             mma_16816(s4[i], a, qlo[kt][0], qlo[kt][1]);
             mma_16816(s4[i], a, qhi[kt][0], qhi[kt][1]);
           }
@@ -493,7 +508,7 @@ decode_kernel(const DecodeParams p) {
           float x = s4[i][j];
           if (p.softcap > 0.f) x = p.softcap * tanhf(x * (p.scale_log2 / kLog2e) / p.softcap) * kLog2e;
           else x *= p.scale_log2;
-          const int r = Q8 ? ((j >> 1) ? q_r1 : q_r0) : g + (j >> 1) * 8;  // stage row
+          const int r = (j >> 1) ? q_r1 : q_r0;  // stage row
           s4[i][j] = key0 + i * kKeys + r < cur.hi ? x : -INFINITY;
         }
         mx0 = fmaxf(mx0, fmaxf(s4[i][0], s4[i][2]));
@@ -570,7 +585,7 @@ decode_kernel(const DecodeParams p) {
 #pragma unroll
           for (int mt = 0; mt < KT; ++mt) {
             uint32_t a[4];
-            ldmatrix_x4_trans(a[0], a[1], a[2], a[3], vbase[i] + vrow * ROWB + (mt * 16 + vcol) * 2);
+            ldmatrix_x4_trans(a[0], a[1], a[2], a[3], vbase[i] + vrow_off + (mt * 16 + vcol) * 2);
             mma_16816(oacc[mt], a, b0, b1);
           }
         }
