@@ -261,6 +261,82 @@ def q8_leg(ab, torch, dev, lens, steps, warmup, stream, seed):
     return e0.elapsed_time(e1) / steps, nbytes
 
 
+def _time(torch, stream, fn, steps, warmup):
+    for _ in range(max(3, warmup)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def cfg4_legs(ab, torch, dev, steps, warmup, stream, seed):
+    """BASELINE config 4 (Gemma-style: 16/8 heads, hd 256, softcap 50, scale
+    1/16, layer pattern 5 sliding-window(1024) : 1 global). Prefill step: one
+    8192-token prefill per layer of the pattern (6 launches). Decode step:
+    B = 8 sequences at context 32768, one decode per layer of the pattern over
+    the same caches (6 decode calls). Returns a dict of both legs."""
+    nq, nkv, hd, S, W, cap, sc = 16, 8, 256, 8192, 1024, 50.0, 1.0 / 16
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(S, nq * hd, generator=g, device=dev).half()
+    K = torch.randn(S, nkv * hd, generator=g, device=dev).half()
+    V = torch.randn(S, nkv * hd, generator=g, device=dev).half()
+    out = torch.empty(S, nq * hd, device=dev, dtype=torch.half)
+
+    def prefill_step():
+        ab.prefill(q, K, V, nq, nkv, hd, scale=sc, softcap=cap, out=out, stream=stream)
+        for _ in range(5):
+            ab.prefill(q, K, V, nq, nkv, hd, scale=sc, softcap=cap, window=W, out=out,
+                       stream=stream)
+
+    p_ms = _time(torch, stream, prefill_step, steps, warmup)
+    f_glob = nq * 2 * hd * S * (S + 1)
+    f_swa = 4 * hd * nq * sum(min(t + 1, W) for t in range(S))
+    p_flops = f_glob + 5 * f_swa
+    del q, K, V, out
+    B, L = 8, 32768
+    Ks = [torch.randn(L, nkv * hd, generator=g, device=dev).half() for _ in range(B)]
+    Vs = [torch.randn(L, nkv * hd, generator=g, device=dev).half() for _ in range(B)]
+    qd = torch.randn(B, nq * hd, generator=g, device=dev)
+    Kt, Vt = ab.ptr_table(Ks, dev), ab.ptr_table(Vs, dev)
+    pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+    od = torch.empty(B, nq * hd, device=dev)
+    ws = ab.Workspace()
+
+    def decode_step():
+        ab.decode(qd, Kt, Vt, pos, nq, nkv, hd, scale=sc, softcap=cap, max_kv_len=L, out=od,
+                  workspace=ws, stream=stream)
+        for _ in range(5):
+            ab.decode(qd, Kt, Vt, pos, nq, nkv, hd, scale=sc, softcap=cap, window=W,
+                      max_kv_len=L, out=od, workspace=ws, stream=stream)
+
+    d_ms = _time(torch, stream, decode_step, steps, warmup)
+    d_bytes = B * nkv * hd * 2 * 2 * (L + 5 * W) + 6 * B * nq * hd * 8
+    return {"prefill_ms": p_ms, "prefill_flops": p_flops, "decode_ms": d_ms,
+            "decode_bytes": d_bytes}
+
+
+def cfg5b_leg(ab, torch, dev, steps, warmup, stream, seed):
+    """BASELINE config 5b: B = 256 sequences of 4096 tokens, 64/8 heads, hd 128,
+    fp16 KV (4.3 GB), one decode per step. Returns (ms, algorithmic bytes)."""
+    nq, nkv, hd, B, L = 64, 8, 128, 256, 4096
+    g = torch.Generator(device=dev).manual_seed(seed)
+    Ks = [torch.randn(L, nkv * hd, generator=g, device=dev).half() for _ in range(B)]
+    Vs = [torch.randn(L, nkv * hd, generator=g, device=dev).half() for _ in range(B)]
+    q = torch.randn(B, nq * hd, generator=g, device=dev)
+    Kt, Vt = ab.ptr_table(Ks, dev), ab.ptr_table(Vs, dev)
+    pos = torch.full((B,), L - 1, dtype=torch.int32, device=dev)
+    out = torch.empty(B, nq * hd, device=dev)
+    ws = ab.Workspace()
+    ms = _time(torch, stream, lambda: ab.decode(q, Kt, Vt, pos, nq, nkv, hd, max_kv_len=L, out=out,
+                                                workspace=ws, stream=stream), steps, warmup)
+    return ms, B * L * nkv * hd * 2 * 2 + B * nq * hd * 8
+
+
 def prefill_cpu_sample(q, K, V, seconds=8.0):
     """CPU oracle on the last rows of one config-3 sequence (causal flops of
     those rows / time), all host cores."""
@@ -453,21 +529,30 @@ def main():
     q_ms, q_bytes = q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4000 + rank)
     if ab.device_status() != 0:
         raise RuntimeError("device status after q8 decode")
+    torch.cuda.empty_cache()
+    x_steps = max(5, min(args.steps, 20))
+    c4 = cfg4_legs(ab, torch, dev, x_steps, args.warmup, stream, 5000 + rank)
+    torch.cuda.empty_cache()
+    b_ms, b_bytes = cfg5b_leg(ab, torch, dev, x_steps, args.warmup, stream, 6000 + rank)
+    torch.cuda.empty_cache()
+    if ab.device_status() != 0:
+        raise RuntimeError("device status after cfg4 / cfg5b")
 
     nbytes = algo_bytes(lens)
-    stats = torch.tensor([ms, ms_e2e, p_ms, l_ms, q_ms, float(nbytes), float(p_flops),
-                          float(l_bytes), float(q_bytes)], dtype=torch.float64, device=dev)
+    times = [ms, ms_e2e, p_ms, l_ms, q_ms, c4["prefill_ms"], c4["decode_ms"], b_ms]
+    work = [float(nbytes), float(p_flops), float(l_bytes), float(q_bytes),
+            float(c4["prefill_flops"]), float(c4["decode_bytes"]), float(b_bytes)]
+    stats = torch.tensor(times + work, dtype=torch.float64, device=dev)
     if dist:
-        mx = stats[:5].clone()
+        mx = stats[:len(times)].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = stats[5:].clone()
+        tot = stats[len(times):].clone()
         dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max = (float(x) for x in mx)
-        bytes_all, flops_all, l_bytes_all, q_bytes_all = (float(x) for x in tot)
+        times_max, work_all = [float(x) for x in mx], [float(x) for x in tot]
     else:
-        ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max = ms, ms_e2e, p_ms, l_ms, q_ms
-        bytes_all, flops_all, l_bytes_all, q_bytes_all = (float(nbytes), float(p_flops),
-                                                          float(l_bytes), float(q_bytes))
+        times_max, work_all = times, work
+    ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max, c4p_max, c4d_max, b_ms_max = times_max
+    bytes_all, flops_all, l_bytes_all, q_bytes_all, c4p_all, c4d_all, b_all = work_all
 
     if rank == 0:
         hbm, src = peaks()
@@ -535,6 +620,28 @@ def main():
                          "peak": peaks()[0], "unit": "GB/s",
                          "frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks()[0], 4)},
             "gpu_launches": args.steps * 2,
+        }
+        hbm_peak, tc_peak = peaks()[0], peaks_tensor()[0]
+        line["cfg4"] = {
+            "metric": "cfg4 (16/8 heads, hd256, softcap 50, 5 SWA(1024) : 1 global): prefill "
+                      "TFLOP/s over 8192 tokens x 6 layers; decode KV GB/s, B=8 at ctx 32768 x 6 "
+                      "layers",
+            "prefill": {"value": round(c4p_all / (c4p_max * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                        "ms_per_step": round(c4p_max, 4),
+                        "frac_of_tensor_peak": round(c4["prefill_flops"] / (c4["prefill_ms"] * 1e-3)
+                                                     / 1e12 / tc_peak, 4)},
+            "decode": {"value": round(c4d_all / (c4d_max * 1e-3) / 1e9, 1), "unit": "GB/s",
+                       "ms_per_step": round(c4d_max, 4),
+                       "frac_of_hbm": round(c4["decode_bytes"] / (c4["decode_ms"] * 1e-3) / 1e9
+                                            / hbm_peak, 4)},
+            "gpu_launches": x_steps * 6 * 3,
+        }
+        line["cfg5b"] = {
+            "metric": "cfg5b decode KV GB/s (B=256 x 4096 tokens, 64/8 heads, hd128, fp16 KV)",
+            "value": round(b_all / (b_ms_max * 1e-3) / 1e9, 1), "unit": "GB/s",
+            "ms_per_step": round(b_ms_max, 4),
+            "frac_of_hbm": round(b_bytes / (b_ms * 1e-3) / 1e9 / hbm_peak, 4),
+            "gpu_launches": x_steps * 2,
         }
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(lens, args.cpu_seconds,

@@ -272,3 +272,20 @@ def test_decode_paged_matches_contiguous(ab, oracle):
     torch.cuda.synchronize()
     ref = oracle_decode(oracle, q, Ks, Vs, [L - 1 for L in lens], nq, nkv, hd)
     assert_parity(got.cpu().numpy(), ref, what="paged")
+
+
+def test_decode_cfg5b_full_size_sampled(ab, oracle):
+    """BASELINE config 5b at full size: B=256 x 4096 tokens, 64/8 heads, hd128
+    (4.3 GB fp16 KV). The whole batch runs in one call; eight sequences spread
+    over the batch are checked against the oracle."""
+    nq, nkv, hd, B, L = 64, 8, 128, 256, 4096
+    g = torch.Generator(device="cuda").manual_seed(55)
+    Ks = [torch.randn(L, nkv * hd, generator=g, device="cuda").half() for _ in range(B)]
+    Vs = [torch.randn(L, nkv * hd, generator=g, device="cuda").half() for _ in range(B)]
+    q = torch.randn(B, nq * hd, generator=g, device="cuda")
+    got = run_decode(ab, q, Ks, Vs, [L - 1] * B, nq, nkv, hd)
+    pick = [0, 1, 37, 100, 128, 199, 254, 255]
+    ref = oracle.decode_batch(q[pick].cpu().numpy(), [Ks[i].float().cpu().numpy() for i in pick],
+                              [Vs[i].float().cpu().numpy() for i in pick], [L - 1] * len(pick),
+                              nq, nkv, hd)
+    assert_parity(got[pick], ref, what="cfg5b")
