@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only warm-up + timed steps of one leg, no clock soak, e2e or CPU")
-    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long", "q8"], default="decode")
+    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long", "q8", "cfg4"], default="decode")
     return ap.parse_args()
 
 
@@ -454,6 +454,10 @@ def main():
         if args.profile_leg == "decode":
             for _ in range(args.steps):
                 step()
+        elif args.profile_leg == "cfg4":
+            for c in caches:
+                c.free()
+            cfg4_legs(ab, torch, dev, args.steps, args.warmup, stream, 5000 + rank)
         elif args.profile_leg == "q8":
             for c in caches:
                 c.free()
