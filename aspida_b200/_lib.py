@@ -30,6 +30,11 @@ SIGNATURES = {
     "aspida_attn_prep": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp, f32, vp, i32, vp, vp,
                                i32, i32, i32, f32, f32, f32, i32, f32, f32, vp, i32, i32, i32,
                                vp]),
+    "aspida_attn_prep_paged": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp, f32, vp, i32, vp,
+                                     vp, vp, i32, i32, i32, vp, i32, f32, f32, f32, i32, f32, f32,
+                                     vp, i32, i32, i32, vp]),
+    "aspida_attn_prefill_paged": (i32, [vp, vp, vp, vp, i32, i32, vp, vp, i32, i32, i32, i32, i32,
+                                        i32, f32, i32, f32, vp]),
     "aspida_attn_decode_workspace_size": (sz, [i32, i32, i32, i32, i32, i32]),
     "aspida_attn_decode": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32, f32,
                                  i32, i32, vp, sz, vp]),

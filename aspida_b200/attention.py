@@ -187,6 +187,30 @@ def prep(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, K: torch.Tensor, V: 
     return q_out
 
 
+def prep_paged(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, K_pool: torch.Tensor,
+               V_pool: torch.Tensor, block_table: torch.Tensor, block_size: int, nq: int,
+               nkv: int, hd: int, rope: RopeParams, *, pos_start: int = 0,
+               pos: Optional[torch.Tensor] = None, q_norm: Optional[torch.Tensor] = None,
+               k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6,
+               q_out_dtype=torch.float32, stream=None) -> torch.Tensor:
+    """prep() appending into paged pools K_pool/V_pool [blocks*block_size,
+    nkv*hd]. pos None: P tokens of one sequence at pos_start.. through the
+    block_table int32 [max_blocks]; pos int32 [P]: a decode batch, row t at
+    pos[t] through block_table row t ([P, max_blocks])."""
+    P = q.shape[0]
+    q_out = torch.empty((P, nq * hd), dtype=q_out_dtype, device=q.device)
+    ff = rope.freq_factors if rope.use_ff else None
+    rc = _lib_().aspida_attn_prep_paged(
+        _ptr(q), _ptr(k), _ptr(v), P, nq, nkv, hd, _ptr(q_norm), _ptr(k_norm), eps,
+        _ptr(q_out), int(q_out_dtype == torch.float16), _ptr(K_pool), _ptr(V_pool),
+        _ptr(block_table), block_table.shape[-1], block_size, pos_start, _ptr(pos),
+        rope.dim, rope.freq_base, rope.freq_scale, rope.m_scale, int(rope.yarn_on),
+        rope.corr_low, rope.corr_high, _ptr(ff), int(rope.use_ff), int(rope.interleaved),
+        rope.sec_total, _stream(stream))
+    _check(rc, "prep_paged")
+    return q_out
+
+
 def ptr_table(tensors: Sequence[torch.Tensor], device) -> torch.Tensor:
     return torch.tensor([t.data_ptr() for t in tensors], dtype=torch.int64, device=device)
 
@@ -360,6 +384,29 @@ def prefill(q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, nq: int, nkv: int
         _ptr(q), _ptr(K), _ptr(V), _ptr(gate), _ptr(out), int(out.dtype == torch.float32), nq,
         nkv, hd, P, pos_start, scale, window, softcap, _stream(stream))
     _check(rc, "prefill")
+    return out
+
+
+def prefill_paged(q: torch.Tensor, K_pool: torch.Tensor, V_pool: torch.Tensor,
+                  block_table: torch.Tensor, block_size: int, nq: int, nkv: int, hd: int,
+                  pos_start: int = 0, *, gate: Optional[torch.Tensor] = None,
+                  scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
+                  out_dtype=torch.float16, out: Optional[torch.Tensor] = None,
+                  stream=None) -> torch.Tensor:
+    """prefill() over paged pools [blocks*block_size, nkv*hd] through
+    block_table int32 [max_blocks]; block_size a multiple of 128 (hd <= 128)
+    or 64 (hd 256)."""
+    P = q.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((P, nq * hd), dtype=out_dtype, device=q.device)
+    nblocks = K_pool.shape[0] // block_size
+    rc = _lib_().aspida_attn_prefill_paged(
+        _ptr(q), _ptr(K_pool), _ptr(V_pool), _ptr(block_table), nblocks, block_size, _ptr(gate),
+        _ptr(out), int(out.dtype == torch.float32), nq, nkv, hd, P, pos_start, scale, window,
+        softcap, _stream(stream))
+    _check(rc, "prefill_paged")
     return out
 
 

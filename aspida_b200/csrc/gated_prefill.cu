@@ -19,7 +19,7 @@ namespace aspida {
 int prefill_batch(int nseq, const void* const* q, const void* const* K, const void* const* V,
                   const float* const* gate, void* const* out, const int* P, const int* pos_start,
                   int out_f32, int nq, int nkv, int hd, float scale, int window, float softcap,
-                  cudaStream_t st);
+                  cudaStream_t st, const int* block_table, int num_blocks, int block_size);
 
 namespace {
 
@@ -74,7 +74,7 @@ extern "C" int aspida_attn_prefill_gated(const float* q_all, const void* K, cons
       const void* qv = qh;
       void* ov = out;
       rc = prefill_batch(1, &qv, &K, &V, gate ? &gate : nullptr, &ov, &P, &pos_start, 1, nq,
-                         nkv, hd, 1.0f / sqrtf((float)hd), 0, 0.0f, st);
+                         nkv, hd, 1.0f / sqrtf((float)hd), 0, 0.0f, st, nullptr, 0, 0);
     }
   }
   if (rc) cudaMemsetAsync(out, 0, (size_t)n * sizeof(float), st);  // never leave `out` stale

@@ -62,10 +62,22 @@ struct PrefillParams {
   const float* gate[kMaxSeq];
   int P[kMaxSeq];
   int pos_start[kMaxSeq];
+  const int* btab[kMaxSeq];         // paged caches: block table per sequence, else null
+  int block_size;                   // rows per block (a multiple of the key-tile height)
   DeviceStatus* status;
   int nq, nkv, G, window, out_f32, ntq;
   float scale_log2, softcap;
 };
+
+// Row of the K/V tensor map holding key row `row` of sequence `seq`: the row
+// itself for a contiguous cache; for a paged cache, its block's pool row
+// (block_table[row / block_size] * block_size + row % block_size). A key
+// tile never crosses a block because block_size is a multiple of its height.
+__device__ __forceinline__ int kv_map_row(const PrefillParams& p, int seq, int row) {
+  const int* bt = p.btab[seq];
+  if (!bt) return row;
+  return __ldg(bt + row / p.block_size) * p.block_size + row % p.block_size;
+}
 
 // tanh(y) = 1 - 2 / (1 + e^{2y}), with e^{2y} = 2^{2y log2 e} from ex2.approx
 // and the reciprocal from rcp.approx: absolute error ~1e-7 (x50 cap: ~5e-6 in
@@ -301,8 +313,11 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
             tc::tma_load_2d(Qs + X * Geo::QT_BYTES + c * BM * 128, &p.qmap[it.seq],
                             it.h * HD + c * 64, it.qt * 2 * BM + X * BM, &sy.q_full);
         ++ic;
+        // key-tile row in the K/V maps, looked up one tile ahead (paged caches)
+        int nrow = it.n > 0 ? kv_map_row(p, it.seq, it.t0 * BN) : 0;
         for (int j = 0; j < it.n; ++j, ++g) {
-          const int s = (int)(g % NS), row = (it.t0 + j) * BN;
+          const int s = (int)(g % NS), row = nrow;
+          if (j + 1 < it.n) nrow = kv_map_row(p, it.seq, (it.t0 + j + 1) * BN);
           if (g >= NS && !wait2(&sy.k_empty[s], ((g / NS) - 1) & 1, sy, p, 20)) break;
           mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
           for (int c = 0; c < CH; ++c)
@@ -714,8 +729,11 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
           tc::tma_load_2d(Qs + c * BM * 128, &p.qmap[it.seq], it.h * HD + c * 64, it.qt * BM,
                           &sy.q_full);
         ++ic;
+        // key-tile row in the K/V maps, looked up one tile ahead (paged caches)
+        int nrow = it.n > 0 ? kv_map_row(p, it.seq, it.x0 * BN) : 0;
         for (int j = 0; j < it.n; ++j, ++g) {
-          const int s = (int)(g % NS), row = (it.x0 + j) * BN;
+          const int s = (int)(g % NS), row = nrow;
+          if (j + 1 < it.n) nrow = kv_map_row(p, it.seq, (it.x0 + j + 1) * BN);
           if (g >= NS && !wait1(&sy.k_empty[s], ((g / NS) - 1) & 1, sy, p, 20)) break;
           mbar_arrive_expect_tx(&sy.k_full[s], Geo::KV_BYTES);
           for (int c = 0; c < CH; ++c)
@@ -1017,14 +1035,23 @@ int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
 
 }  // namespace
 
+// Paged form (block_table != null, one sequence): K/V are pools of num_blocks
+// blocks of block_size rows.
 int prefill_batch(int nseq, const void* const* q, const void* const* K, const void* const* V,
                   const float* const* gate, void* const* out, const int* P, const int* pos_start,
                   int out_f32, int nq, int nkv, int hd, float scale, int window, float softcap,
-                  cudaStream_t st) {
+                  cudaStream_t st, const int* block_table = nullptr, int num_blocks = 0,
+                  int block_size = 0) {
   if (nseq <= 0) return 0;
   if (!q || !K || !V || !out || !P || !pos_start || nq <= 0 || nkv <= 0 || nq % nkv)
     return record_status(ASPIDA_ERR_ARG);
   if (hd != 64 && hd != 128 && hd != 256) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  const int tile_rows = hd <= 128 ? 128 : 64;       // key-tile height of the kernel
+  if (block_table) {
+    if (nseq != 1 || num_blocks <= 0 || block_size <= 0) return record_status(ASPIDA_ERR_ARG);
+    if (block_size % tile_rows) return record_status(ASPIDA_ERR_UNSUPPORTED);
+    if ((long)num_blocks * block_size >= (1L << 31)) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  }
   for (int base = 0; base < nseq; base += kMaxSeq) {
     const int cnt = std::min(kMaxSeq, nseq - base);
     PrefillParams p;
@@ -1038,10 +1065,12 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
       if (((uintptr_t)q[s] | (uintptr_t)K[s] | (uintptr_t)V[s] | (uintptr_t)out[s]) & 15)
         return record_status(ASPIDA_ERR_ARG);
       const int Pv = std::max(P[s], 1), len = pos_start[s] + Pv;
+      const int kv_rows = block_table ? num_blocks * block_size : len;
       if (!make_map(&p.qmap[i], q[s], (long)nq * hd, Pv, BM) ||
-          !make_map(&p.kmap[i], K[s], (long)nkv * hd, len, box_kv) ||
-          !make_map(&p.vmap[i], V[s], (long)nkv * hd, len, box_kv))
+          !make_map(&p.kmap[i], K[s], (long)nkv * hd, kv_rows, box_kv) ||
+          !make_map(&p.vmap[i], V[s], (long)nkv * hd, kv_rows, box_kv))
         return record_status(ASPIDA_ERR_ARG);
+      p.btab[i] = block_table;
       if (!out_f32 && !make_map(&p.omap[i], out[s], (long)nq * hd, Pv, BM))
         return record_status(ASPIDA_ERR_ARG);
       p.out[i] = out[s];
@@ -1052,6 +1081,7 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     }
     if (maxP == 0) continue;
     p.status = device_status_ptr();
+    p.block_size = block_size;
     p.nq = nq; p.nkv = nkv; p.G = nq / nkv;
     p.window = window; p.out_f32 = out_f32;
     p.scale_log2 = scale * kLog2e;
@@ -1078,6 +1108,17 @@ extern "C" int aspida_attn_prefill(const void* q, const void* K, const void* V, 
   return aspida::prefill_batch(1, &q, &K, &V, gate ? &gate : nullptr, &out, &P, &pos_start,
                                out_f32, nq, nkv, hd, scale, window, softcap,
                                (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_prefill_paged(const void* q, const void* K_pool, const void* V_pool,
+                                         const int* block_table, int num_blocks, int block_size,
+                                         const float* gate, void* out, int out_f32, int nq,
+                                         int nkv, int hd, int P, int pos_start, float scale,
+                                         int window, float softcap, void* stream) {
+  if (!block_table) return aspida::record_status(ASPIDA_ERR_ARG);
+  return aspida::prefill_batch(1, &q, &K_pool, &V_pool, gate ? &gate : nullptr, &out, &P,
+                               &pos_start, out_f32, nq, nkv, hd, scale, window, softcap,
+                               (cudaStream_t)stream, block_table, num_blocks, block_size);
 }
 
 extern "C" int aspida_attn_prefill_batch(int nseq, const void* const* q, const void* const* K,

@@ -39,7 +39,8 @@ __global__ void prep_kernel(const float* __restrict__ q, const float* __restrict
                             int max_len, const int* max_len_tab, int pos_start,
                             const int* pos_tab, int rd, float base, float freq_scale, float m_scale,
                             int yarn_on, float corr_lo, float corr_hi, const float* __restrict__ ff,
-                            int use_ff, int interleaved, int sec_total) {
+                            int use_ff, int interleaved, int sec_total,
+                            const int* __restrict__ btab, int max_blocks, int block_size) {
   extern __shared__ float sh[];  // [hd]
   const int t = blockIdx.x, head = blockIdx.y, d = threadIdx.x;
   // Row t is either token t of one sequence (consecutive positions, one
@@ -51,9 +52,15 @@ __global__ void prep_kernel(const float* __restrict__ q, const float* __restrict
   const int kvh = head - nq;
   const long kvd = (long)nkv * hd, att = (long)nq * hd;
   if (!is_q && (pos < 0 || pos >= max_len)) return;  // never write past the cache
+  // cache row of this position: itself, or (paged) its block's pool row
+  long row = pos;
+  if (btab && !is_q) {
+    const int* bt = btab + (pos_tab ? (long)t * max_blocks : 0);
+    row = (long)bt[pos / block_size] * block_size + pos % block_size;
+  }
 
   float x = is_q ? q[t * att + (long)head * hd + d] : k[t * kvd + (long)kvh * hd + d];
-  if (!is_q) Vc[(long)pos * kvd + (long)kvh * hd + d] = __float2half_rn(v[t * kvd + (long)kvh * hd + d]);
+  if (!is_q) Vc[row * kvd + (long)kvh * hd + d] = __float2half_rn(v[t * kvd + (long)kvh * hd + d]);
 
   const float* nw = is_q ? q_norm : k_norm;
   sh[d] = x;
@@ -99,7 +106,7 @@ __global__ void prep_kernel(const float* __restrict__ q, const float* __restrict
     if (q_out_fp16) static_cast<__half*>(q_out)[idx] = __float2half_rn(o);
     else static_cast<float*>(q_out)[idx] = o;
   } else {
-    Kc[(long)pos * kvd + (long)kvh * hd + d] = __float2half_rn(o);
+    Kc[row * kvd + (long)kvh * hd + d] = __float2half_rn(o);
   }
 }
 
@@ -118,8 +125,8 @@ int launch_prep(const float* q, const float* k, const float* v, int P, int nq, i
   dim3 grid(P, nq + nkv);
   prep_kernel<<<grid, hd, hd * sizeof(float), st>>>(
       q, k, v, nq, nkv, hd, q_norm, k_norm, eps, q_out, q_out_fp16, (__half*)K, (__half*)V,
-      nullptr, nullptr, max_len, nullptr, pos_start, nullptr, rd, base, freq_scale, m_scale, yarn_on, corr_lo, corr_hi, ff, use_ff,
-      interleaved, sec_total);
+      nullptr, nullptr, max_len, nullptr, pos_start, nullptr, rd, base, freq_scale, m_scale,
+      yarn_on, corr_lo, corr_hi, ff, use_ff, interleaved, sec_total, nullptr, 0, 1);
   ASPIDA_CHECK_LAUNCH();
   return 0;
 }
@@ -135,12 +142,54 @@ int launch_prep_lanes(const float* q, const float* k, const float* v, int B, int
     return record_status(ASPIDA_ERR_ARG);
   prep_kernel<<<dim3(B, nq + nkv), hd, hd * sizeof(float), st>>>(
       q, k, v, nq, nkv, hd, nullptr, nullptr, 0.f, q_out, 0, nullptr, nullptr, Ktab, Vtab, 0,
-      max_len, 0, pos, rd, base, 1.0f, 1.0f, 0, 0.f, 0.f, nullptr, 0, interleaved, rd / 2);
+      max_len, 0, pos, rd, base, 1.0f, 1.0f, 0, 0.f, 0.f, nullptr, 0, interleaved, rd / 2,
+      nullptr, 0, 1);
+  ASPIDA_CHECK_LAUNCH();
+  return 0;
+}
+
+// Paged form: K/V are block pools; row t appends at pos[t] through block-table
+// row t (pos != null, a decode batch) or at pos_start + t through one table.
+int launch_prep_paged(const float* q, const float* k, const float* v, int P, int nq, int nkv,
+                      int hd, const float* q_norm, const float* k_norm, float eps, void* q_out,
+                      int q_out_fp16, void* K_pool, void* V_pool, const int* block_table,
+                      int max_blocks, int block_size, int pos_start, const int* pos, int rd,
+                      float base, float freq_scale, float m_scale, int yarn_on, float corr_lo,
+                      float corr_hi, const float* ff, int use_ff, int interleaved, int sec_total,
+                      cudaStream_t st) {
+  if (P <= 0) return 0;
+  if (!q || !k || !v || !q_out || !K_pool || !V_pool || !block_table || nq <= 0 || nkv <= 0 ||
+      nq % nkv != 0 || hd <= 0 || hd > 1024 || rd < 0 || rd > hd || (rd & 1) ||
+      (use_ff && !ff) || max_blocks <= 0 || block_size <= 0 ||
+      (long)max_blocks * block_size >= (1L << 31) ||
+      (!pos && (pos_start < 0 || (long)pos_start + P > (long)max_blocks * block_size)))
+    return record_status(ASPIDA_ERR_ARG);
+  prep_kernel<<<dim3(P, nq + nkv), hd, hd * sizeof(float), st>>>(
+      q, k, v, nq, nkv, hd, q_norm, k_norm, eps, q_out, q_out_fp16, (__half*)K_pool,
+      (__half*)V_pool, nullptr, nullptr, max_blocks * block_size, nullptr, pos_start, pos, rd,
+      base, freq_scale, m_scale, yarn_on, corr_lo, corr_hi, ff, use_ff, interleaved, sec_total,
+      block_table, max_blocks, block_size);
   ASPIDA_CHECK_LAUNCH();
   return 0;
 }
 
 }  // namespace aspida
+
+extern "C" int aspida_attn_prep_paged(const float* q, const float* k, const float* v, int P,
+                                      int nq, int nkv, int hd, const float* q_norm,
+                                      const float* k_norm, float eps, void* q_out,
+                                      int q_out_fp16, void* K_pool, void* V_pool,
+                                      const int* block_table, int max_blocks, int block_size,
+                                      int pos_start, const int* pos, int rd, float base,
+                                      float freq_scale, float m_scale, int yarn_on,
+                                      float corr_lo, float corr_hi, const float* ff, int use_ff,
+                                      int interleaved, int sec_total, void* stream) {
+  return aspida::launch_prep_paged(q, k, v, P, nq, nkv, hd, q_norm, k_norm, eps, q_out,
+                                   q_out_fp16, K_pool, V_pool, block_table, max_blocks,
+                                   block_size, pos_start, pos, rd, base, freq_scale, m_scale,
+                                   yarn_on, corr_lo, corr_hi, ff, use_ff, interleaved, sec_total,
+                                   (cudaStream_t)stream);
+}
 
 extern "C" int aspida_attn_prep(const float* q, const float* k, const float* v, int P, int nq,
                                 int nkv, int hd, const float* q_norm, const float* k_norm,

@@ -107,6 +107,21 @@ int aspida_attn_prep(const float* q, const float* k, const float* v, int P, int 
                      float corr_hi, const float* ff, int use_ff, int interleaved, int sec_total,
                      void* stream);
 
+/* Paged form of aspida_attn_prep: K_pool / V_pool are fp16 pools of blocks of
+ * block_size rows ([blocks*block_size][nkv*hd]); the new rows go to
+ * block_table[pos / block_size] * block_size + pos % block_size, the KV_Pool
+ * block tables of src/llm/kv_pool.ads:1-47. pos == NULL: P tokens of one
+ * sequence at pos_start.. through block_table [max_blocks]; pos != NULL
+ * (dev i32 [P]): a decode batch, row t at pos[t] through block_table row t
+ * ([P][max_blocks]). Positions must lie below max_blocks*block_size. */
+int aspida_attn_prep_paged(const float* q, const float* k, const float* v, int P, int nq, int nkv,
+                           int hd, const float* q_norm, const float* k_norm, float eps,
+                           void* q_out, int q_out_fp16, void* K_pool, void* V_pool,
+                           const int* block_table, int max_blocks, int block_size, int pos_start,
+                           const int* pos, int rd, float base, float freq_scale, float m_scale,
+                           int yarn_on, float corr_lo, float corr_hi, const float* ff,
+                           int use_ff, int interleaved, int sec_total, void* stream);
+
 /* ------------------------------------------------------------------------
  * Decode attention (one new token per sequence, GQA, split-KV).
  * Replaces the k_fattn_attend / k_fattn_attend_b launches
@@ -217,6 +232,19 @@ int aspida_attn_merge_strided(const float* m, const float* l, const float* o, co
 int aspida_attn_prefill(const void* q, const void* K, const void* V, const float* gate, void* out,
                         int out_f32, int nq, int nkv, int hd, int P, int pos_start, float scale,
                         int window, float softcap, void* stream);
+
+/* Paged form of aspida_attn_prefill: K_pool / V_pool hold num_blocks blocks
+ * of block_size rows; key row r of the sequence lives in pool row
+ * block_table[r / block_size] * block_size + r % block_size (dev i32 table).
+ * block_size must be a multiple of the kernel's key tile (128 for hd <= 128,
+ * 64 for hd 256), else ASPIDA_ERR_UNSUPPORTED. Rows of the last block past
+ * pos_start + P are read (with zero weight), so they must hold finite values
+ * (a zero-initialised pool does). */
+int aspida_attn_prefill_paged(const void* q, const void* K_pool, const void* V_pool,
+                              const int* block_table, int num_blocks, int block_size,
+                              const float* gate, void* out, int out_f32, int nq, int nkv, int hd,
+                              int P, int pos_start, float scale, int window, float softcap,
+                              void* stream);
 
 /* Batched form: nseq sequences, each with its own q/K/V/gate/out pointers
  * and P / pos_start (host arrays of device pointers and host ints). */
