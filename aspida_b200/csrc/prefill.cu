@@ -122,6 +122,34 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
+// 2^x for both lanes of an f32 pair on the FMA and integer pipes instead of
+// the MUFU unit (the softmax is MUFU-bound: two 128 x 128 score tiles need
+// ~2048 MUFU cycles per key tile, as long as the tile's MMAs). Cody-Waite
+// range reduction: n = round(x) with the 1.5 * 2^23 shifter (n lands in the
+// low mantissa bits), f = x - n in [-0.5, 0.5], 2^f from a degree-3
+// polynomial (weighted least squares at Chebyshev nodes, exp2_poly_fit.py;
+// max relative error 7.7e-5, below the fp16 rounding of P), and 2^n added
+// to the exponent field. x is clamped to [-126, ...): masked (-inf) scores
+// give ~1e-38, which rounds to 0 in fp16. Inputs are at most 2^8 here.
+#ifndef ASPIDA_EXP2_POLY_EVERY
+#define ASPIDA_EXP2_POLY_EVERY 4     // one score pair in 4 takes this path
+#endif
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+  float2 v = f2_unpack(x);
+  v.x = fmaxf(v.x, -126.f);
+  v.y = fmaxf(v.y, -126.f);
+  const uint64_t xc = f2_pack(v.x, v.y);
+  const uint64_t t = f2_add(xc, f2_pack(12582912.f, 12582912.f));
+  const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
+  const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), xc);
+  uint64_t p = f2_fma(f2_pack(0.055088684f, 0.055088684f), f, f2_pack(0.242604047f, 0.242604047f));
+  p = f2_fma(p, f, f2_pack(0.693276227f, 0.693276227f));
+  p = f2_fma(p, f, f2_pack(0.999928951f, 0.999928951f));
+  const float2 tv = f2_unpack(t), pv = f2_unpack(p);
+  return f2_pack(__uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23)),
+                 __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23)));
+}
+
 // max(a, b, c) in one instruction (sm_100 three-input max).
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float d;
@@ -498,8 +526,17 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float2 a = f2_unpack(f2_fma(f2_pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sc2, nm2));
-            const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
+            const uint64_t a2 = f2_fma(f2_pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sc2, nm2);
+            float e0, e1;
+            if (ASPIDA_EXP2_POLY_EVERY > 0 && i % ASPIDA_EXP2_POLY_EVERY == ASPIDA_EXP2_POLY_EVERY - 1) {
+              const float2 e = f2_unpack(f2_exp2_poly(a2));
+              e0 = e.x;
+              e1 = e.y;
+            } else {
+              const float2 a = f2_unpack(a2);
+              e0 = fast_exp2(a.x);
+              e1 = fast_exp2(a.y);
+            }
             sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(e0, e1));
             pk[i] = pack_half2(e0, e1);
           }
