@@ -1,10 +1,12 @@
-"""Coefficients of the degree-3 polynomial p(f) ~ 2^f on [-0.5, 0.5] used by
-the prefill softmax's FMA-pipe exponential (prefill.cu, f2_exp2_poly).
+"""Coefficients of the polynomials p(f) ~ 2^f on [-0.5, 0.5] used by the
+prefill kernels' FMA-pipe exponentials (prefill.cu, f2_exp2_poly): degree 3
+for the softmax, degree 4 for the softcap's tanh.
 
 Method: weighted least squares (relative error) at 2000 Chebyshev nodes,
 rounded to float32; the script prints the coefficients and the maximum
-relative error of the float32 Horner evaluation (7.7e-5, below the 4.9e-4
-rounding of the fp16 P operand). Run: python aspida_b200/csrc/exp2_poly_fit.py
+relative error of the float32 Horner evaluation: degree 3 7.7e-5 (below the
+4.9e-4 rounding of the fp16 P operand), degree 4 2.7e-6 (tanh error at most
+1.4e-6, 7e-5 in a score capped at 50). Run: python aspida_b200/csrc/exp2_poly_fit.py
 """
 import numpy as np
 
@@ -27,6 +29,7 @@ def max_rel_err(c):
 
 
 if __name__ == "__main__":
-    c = fit()
-    print("coefficients c0..c3:", ", ".join(f"{float(v):.9g}f" for v in c))
-    print("max relative error:", max_rel_err(c))
+    for deg in (3, 4):
+        c = fit(deg)
+        print(f"degree {deg}: coefficients c0..c{deg}:", ", ".join(f"{float(v):.9g}f" for v in c))
+        print("  max relative error:", max_rel_err(c))

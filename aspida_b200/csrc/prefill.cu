@@ -79,27 +79,6 @@ __device__ __forceinline__ int kv_map_row(const PrefillParams& p, int seq, int r
   return __ldg(bt + row / p.block_size) * p.block_size + row % p.block_size;
 }
 
-// tanh(y) = 1 - 2 / (1 + e^{2y}), with e^{2y} = 2^{2y log2 e} from ex2.approx
-// and the reciprocal from rcp.approx: absolute error ~1e-7 (x50 cap: ~5e-6 in
-// the score), with no cancellation problem near 0 at that absolute scale.
-__device__ __forceinline__ float tanh_via_exp2(float y) {
-  const float e = fast_exp2(fminf(2.f * kLog2e * y, 126.f));
-  float r;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(1.f + e));
-  return fmaf(-2.f, r, 1.f);
-}
-
-__device__ __forceinline__ void scores_log2(float* x, bool capped, float cap, float scale_log2) {
-  if (capped) {
-    const float sc = scale_log2 / kLog2e / cap, cl = cap * kLog2e;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] = cl * tanh_via_exp2(x[i] * sc);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) x[i] *= scale_log2;
-  }
-}
-
 // Packed f32x2 arithmetic (sm_100): two lanes of fp32 per instruction.
 __device__ __forceinline__ uint64_t f2_pack(float a, float b) {
   uint64_t r;
@@ -123,31 +102,69 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
 }
 
 // 2^x for both lanes of an f32 pair on the FMA and integer pipes instead of
-// the MUFU unit (the softmax is MUFU-bound: two 128 x 128 score tiles need
-// ~2048 MUFU cycles per key tile, as long as the tile's MMAs). Cody-Waite
-// range reduction: n = round(x) with the 1.5 * 2^23 shifter (n lands in the
-// low mantissa bits), f = x - n in [-0.5, 0.5], 2^f from a degree-3
-// polynomial (weighted least squares at Chebyshev nodes, exp2_poly_fit.py;
-// max relative error 7.7e-5, below the fp16 rounding of P), and 2^n added
-// to the exponent field. x is clamped to [-126, ...): masked (-inf) scores
-// give ~1e-38, which rounds to 0 in fp16. Inputs are at most 2^8 here.
-#ifndef ASPIDA_EXP2_POLY_EVERY
-#define ASPIDA_EXP2_POLY_EVERY 4     // one score pair in 4 takes this path
-#endif
+// the MUFU unit. Cody-Waite range reduction: n = round(x) with the 1.5 * 2^23
+// shifter (n lands in the low mantissa bits), f = x - n in [-0.5, 0.5], 2^f
+// from a polynomial (weighted least squares at Chebyshev nodes,
+// exp2_poly_fit.py), and 2^n added to the exponent field. x is clamped to
+// [-126, 64]: masked (-inf) scores give ~1e-38, which rounds to 0 in fp16.
+//   DEG 3 (softmax P): max relative error 7.7e-5, below P's fp16 rounding.
+//   DEG 4 (softcap tanh): 2.7e-6.
+template <int DEG>
 __device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
   float2 v = f2_unpack(x);
-  v.x = fmaxf(v.x, -126.f);
-  v.y = fmaxf(v.y, -126.f);
+  v.x = fminf(fmaxf(v.x, -126.f), 64.f);
+  v.y = fminf(fmaxf(v.y, -126.f), 64.f);
   const uint64_t xc = f2_pack(v.x, v.y);
   const uint64_t t = f2_add(xc, f2_pack(12582912.f, 12582912.f));
   const uint64_t n = f2_add(t, f2_pack(-12582912.f, -12582912.f));
   const uint64_t f = f2_fma(n, f2_pack(-1.f, -1.f), xc);
-  uint64_t p = f2_fma(f2_pack(0.055088684f, 0.055088684f), f, f2_pack(0.242604047f, 0.242604047f));
-  p = f2_fma(p, f, f2_pack(0.693276227f, 0.693276227f));
-  p = f2_fma(p, f, f2_pack(0.999928951f, 0.999928951f));
+  uint64_t p;
+  if constexpr (DEG == 3) {
+    p = f2_fma(f2_pack(0.055088684f, 0.055088684f), f, f2_pack(0.242604047f, 0.242604047f));
+    p = f2_fma(p, f, f2_pack(0.693276227f, 0.693276227f));
+    p = f2_fma(p, f, f2_pack(0.999928951f, 0.999928951f));
+  } else {
+    p = f2_fma(f2_pack(0.00956051052f, 0.00956051052f), f, f2_pack(0.0559170395f, 0.0559170395f));
+    p = f2_fma(p, f, f2_pack(0.240249813f, 0.240249813f));
+    p = f2_fma(p, f, f2_pack(0.69312197f, 0.69312197f));
+    p = f2_fma(p, f, f2_pack(0.999999166f, 0.999999166f));
+  }
   const float2 tv = f2_unpack(t), pv = f2_unpack(p);
   return f2_pack(__uint_as_float(__float_as_uint(pv.x) + (__float_as_uint(tv.x) << 23)),
                  __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23)));
+}
+
+// The softmax is MUFU-bound (two 128 x 128 score tiles need ~2048 MUFU
+// cycles per key tile, as long as the tile's MMAs): one score pair in
+// ASPIDA_EXP2_POLY_EVERY takes the polynomial path.
+#ifndef ASPIDA_EXP2_POLY_EVERY
+#define ASPIDA_EXP2_POLY_EVERY 4
+#endif
+
+// Softcapped scores in log2 units: x <- cap * log2(e) * tanh(x * scale / cap),
+// with tanh(y) = 1 - 2 / (1 + e^{2y}); e^{2y} from the degree-4 FMA-pipe
+// exponential (taking one of the three MUFU operations per score off the
+// MUFU unit) and the reciprocal from rcp.approx. Absolute tanh error ~2e-6
+// (x50 cap: ~1e-4 in the score), no cancellation near 0 at that scale.
+__device__ __forceinline__ void scores_log2(float* x, bool capped, float cap, float scale_log2) {
+  if (capped) {
+    const float sc2 = 2.f * scale_log2 / cap, cl = cap * kLog2e;   // 2y log2(e) = x * sc2
+    const uint64_t s2 = f2_pack(sc2, sc2);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const uint64_t e2 = f2_exp2_poly<4>(f2_fma(f2_pack(x[2 * i], x[2 * i + 1]), s2,
+                                                 f2_pack(0.f, 0.f)));
+      const float2 e = f2_unpack(e2);
+      float r0, r1;
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(1.f + e.x));
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(1.f + e.y));
+      x[2 * i] = cl * fmaf(-2.f, r0, 1.f);
+      x[2 * i + 1] = cl * fmaf(-2.f, r1, 1.f);
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[i] *= scale_log2;
+  }
 }
 
 // max(a, b, c) in one instruction (sm_100 three-input max).
@@ -529,7 +546,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
             const uint64_t a2 = f2_fma(f2_pack(s[c * 32 + 2 * i], s[c * 32 + 2 * i + 1]), sc2, nm2);
             float e0, e1;
             if (ASPIDA_EXP2_POLY_EVERY > 0 && i % ASPIDA_EXP2_POLY_EVERY == ASPIDA_EXP2_POLY_EVERY - 1) {
-              const float2 e = f2_unpack(f2_exp2_poly(a2));
+              const float2 e = f2_unpack(f2_exp2_poly<3>(a2));
               e0 = e.x;
               e1 = e.y;
             } else {
@@ -907,8 +924,17 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float2 a = f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2));
-          const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
+          const uint64_t a2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
+          float e0, e1;
+          if (ASPIDA_EXP2_POLY_EVERY > 0 && i % ASPIDA_EXP2_POLY_EVERY == ASPIDA_EXP2_POLY_EVERY - 1) {
+            const float2 e = f2_unpack(f2_exp2_poly<3>(a2));
+            e0 = e.x;
+            e1 = e.y;
+          } else {
+            const float2 a = f2_unpack(a2);
+            e0 = fast_exp2(a.x);
+            e1 = fast_exp2(a.y);
+          }
           sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(e0, e1));
           pk[i] = pack_half2(e0, e1);
         }
