@@ -134,9 +134,10 @@ __device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
                  __uint_as_float(__float_as_uint(pv.y) + (__float_as_uint(tv.y) << 23)));
 }
 
-// The softmax is MUFU-bound (two 128 x 128 score tiles need ~2048 MUFU
-// cycles per key tile, as long as the tile's MMAs): one score pair in
-// ASPIDA_EXP2_POLY_EVERY takes the polynomial path.
+// The two-tile kernel's softmax is MUFU-bound (two 128 x 128 score tiles need
+// ~2048 MUFU cycles per key tile, as long as the tile's MMAs): one score pair
+// in ASPIDA_EXP2_POLY_EVERY takes the polynomial path (config 3: +2%; the
+// same split in the hd-256 kernel measured no gain).
 #ifndef ASPIDA_EXP2_POLY_EVERY
 #define ASPIDA_EXP2_POLY_EVERY 4
 #endif
@@ -924,17 +925,8 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const uint64_t a2 = f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2);
-          float e0, e1;
-          if (ASPIDA_EXP2_POLY_EVERY > 0 && i % ASPIDA_EXP2_POLY_EVERY == ASPIDA_EXP2_POLY_EVERY - 1) {
-            const float2 e = f2_unpack(f2_exp2_poly<3>(a2));
-            e0 = e.x;
-            e1 = e.y;
-          } else {
-            const float2 a = f2_unpack(a2);
-            e0 = fast_exp2(a.x);
-            e1 = fast_exp2(a.y);
-          }
+          const float2 a = f2_unpack(f2_fma(f2_pack(s[2 * i], s[2 * i + 1]), sc2, nm2));
+          const float e0 = fast_exp2(a.x), e1 = fast_exp2(a.y);
           sum2[i & 3] = f2_add(sum2[i & 3], f2_pack(e0, e1));
           pk[i] = pack_half2(e0, e1);
         }
