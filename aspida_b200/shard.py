@@ -9,10 +9,16 @@ gradient exchange for training, gpu/dp_node.cu), so these are new parts:
 * Single long-sequence decode splits the KV cache into contiguous chunks
   (``kv_chunks``); each rank attends its chunk and produces the split-KV
   partial (m, l, o) per query head (aspida_attn_decode_partial), the ranks
-  exchange the partials with one all-gather over NCCL, and every rank merges
-  them with the log-sum-exp merge of gpu/fattn_sk.cu:84-97
-  (aspida_attn_merge). The payload is nq*(hd+2) floats per sequence per rank
-  (33 KB at 64 heads x hd 128), so the exchange is latency-bound.
+  exchange the partials and every rank merges them with the log-sum-exp
+  merge of gpu/fattn_sk.cu:84-97. The payload is nq*(hd+2) floats per
+  sequence per rank (33 KB at 64 heads x hd 128), so the exchange is
+  latency-bound. Two transports:
+    - "p2p" (default): one kernel stores this rank's partial into every
+      rank's receive buffer over NVLink (buffers shared once through CUDA IPC
+      handles, :class:`PeerExchange`), waits for all ranks' partials of the
+      step and merges (aspida_attn_exchange_merge);
+    - "nccl": an all-gather of the packed partials, then
+      aspida_attn_merge_strided.
 
 Failures: a collective that fails (a rank died or timed out) raises
 :class:`ShardError`; no rank waits forever, the process-group timeout bounds
@@ -89,19 +95,98 @@ def exchange_partials(m, l, o, group=None) -> Tuple[torch.Tensor, torch.Tensor, 
     return unpack_partials(gathered, world, B, nq, hd)
 
 
+class PeerExchange:
+    """Per-rank NVLink receive buffers for the fused exchange + merge.
+
+    Each rank allocates its buffer in the library (zero-filled) and shares its
+    CUDA IPC handle with the group once; every rank then maps every other
+    rank's buffer. ``__call__`` runs one step: all ranks must call it once per
+    step, in the same order (the step number tags the arrivals)."""
+
+    def __init__(self, rows: int, hd: int, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import _lib
+        from .attention import GPUError
+        self._C, self._lib, self.group = C, _lib.load(), group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("the peer exchange supports up to 8 ranks")
+        self.rows, self.hd, self.step = rows, hd, 0
+        nbytes = self._lib.aspida_attn_peer_buffer_size(self.world, rows, hd)
+        own = C.c_void_p()
+        handle = (C.c_char * 64)()
+        rc = self._lib.aspida_attn_peer_alloc(nbytes, C.byref(own), handle)
+        if rc:
+            raise GPUError(rc, "peer_alloc")
+        self._own = own.value
+        handles = [None] * self.world
+        try:
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        except Exception as e:
+            self._lib.aspida_attn_peer_free(self._own)
+            raise ShardError(f"peer handle exchange failed: {e}") from e
+        ptrs, self._mapped = [], []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                ptrs.append(self._own)
+                continue
+            p = C.c_void_p()
+            rc = self._lib.aspida_attn_peer_open((C.c_char * 64).from_buffer_copy(h), C.byref(p))
+            if rc:
+                self.close()
+                raise GPUError(rc, "peer_open")
+            self._mapped.append(p.value)
+            ptrs.append(p.value)
+        self.table = (C.c_void_p * self.world)(*ptrs)
+
+    def __call__(self, part: torch.Tensor, out: torch.Tensor, gate: Optional[torch.Tensor] = None,
+                 stream=None) -> torch.Tensor:
+        from .attention import GPUError, _stream
+        self.step += 1
+        rc = self._lib.aspida_attn_exchange_merge(
+            part.data_ptr(), self.table, self.world, self.rank, self.step,
+            None if gate is None else gate.data_ptr(), out.data_ptr(), self.rows, self.hd,
+            _stream(stream))
+        if rc:
+            raise GPUError(rc, "exchange_merge")
+        return out
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after a barrier, so
+        no rank still stores into it)."""
+        import torch.distributed as dist
+        if getattr(self, "_own", None) is None:
+            return
+        torch.cuda.synchronize()
+        try:
+            dist.barrier(group=self.group)
+        except Exception:
+            pass
+        for p in self._mapped:
+            self._lib.aspida_attn_peer_close(p)
+        self._mapped = []
+        self._lib.aspida_attn_peer_free(self._own)
+        self._own = None
+
+
 class SeqParallelDecode:
     """Sequence-parallel decode with every buffer allocated once.
 
     Per call: the split-KV partial kernel writes this rank's (m, l, o) straight
-    into a packed send buffer [m | l | o]; one all-gather (NCCL) fills the
-    receive buffer [world][m | l | o]; the strided merge kernel reads it in
-    place. No host synchronisation and no extra device copies.
+    into a packed send buffer [m | l | o]; then, with transport "p2p", one
+    kernel exchanges it over NVLink and merges (:class:`PeerExchange`); with
+    "nccl", one all-gather fills the receive buffer [world][m | l | o] and the
+    strided merge kernel reads it in place. No host synchronisation and no
+    extra device copies. ``close()`` releases the peer buffers.
 
     K_chunks / V_chunks: this rank's fp16 chunk [rows >= n_local, nkv*hd] of
     each of the B sequences' caches; rows 0..n_local-1 are attended."""
 
     def __init__(self, K_chunks, V_chunks, n_local: int, nq: int, nkv: int, hd: int, *,
-                 scale: Optional[float] = None, softcap: float = 0.0, group=None):
+                 scale: Optional[float] = None, softcap: float = 0.0, group=None,
+                 transport: str = "p2p"):
         import math
         import torch.distributed as dist
         from . import attention as ab
@@ -123,6 +208,15 @@ class SeqParallelDecode:
         nbytes = ab.decode_workspace_size(self.B, nq, nkv, hd, max(1, n_local))
         self.ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
         self.pos = torch.full((self.B,), n_local - 1, dtype=torch.int32, device=dev)
+        if transport not in ("p2p", "nccl"):
+            raise ValueError("transport must be 'p2p' or 'nccl'")
+        self.transport = transport if self.world > 1 else "local"
+        self.px = PeerExchange(self.rows, hd, group) if self.transport == "p2p" else None
+
+    def close(self):
+        if self.px is not None:
+            self.px.close()
+            self.px = None
 
     def __call__(self, q: torch.Tensor, gate: Optional[torch.Tensor] = None,
                  stream=None) -> torch.Tensor:
@@ -148,6 +242,8 @@ class SeqParallelDecode:
             self.ws.numel(), st)
         if rc:
             raise GPUError(rc, "decode_partial")
+        if self.transport == "p2p":
+            return self.px(self.send, self.out, gate=gate, stream=stream)
         src = self.send
         if self.world > 1:
             import torch.distributed as dist
@@ -168,7 +264,7 @@ class SeqParallelDecode:
 def seq_parallel_decode(q: torch.Tensor, K_local, V_local, n_local: int, nq: int, nkv: int,
                         hd: int, *, gate: Optional[torch.Tensor] = None,
                         scale: Optional[float] = None, softcap: float = 0.0,
-                        group=None) -> torch.Tensor:
+                        group=None, transport: str = "p2p") -> torch.Tensor:
     """One-shot form of :class:`SeqParallelDecode`. q [B, nq*hd] f32 (identical
     on every rank); K_local / V_local: one tensor when B = 1, else a sequence
     of B chunks. Returns the merged [B, nq*hd] output on every rank."""
@@ -177,5 +273,8 @@ def seq_parallel_decode(q: torch.Tensor, K_local, V_local, n_local: int, nq: int
     if len(Ks) != q.shape[0] or len(Vs) != q.shape[0]:
         raise ValueError("one K/V chunk per sequence")
     op = SeqParallelDecode(Ks, Vs, n_local, nq, nkv, hd, scale=scale, softcap=softcap,
-                           group=group)
-    return op(q, gate=gate).clone()
+                           group=group, transport=transport)
+    try:
+        return op(q, gate=gate).clone()
+    finally:
+        op.close()

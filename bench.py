@@ -193,8 +193,8 @@ def prefill_leg(ab, torch, dev, seed, steps, warmup, stream):
 def long_leg(ab, torch, dev, rank, world, steps, warmup, stream, dist):
     """BASELINE config 5a: one 131072-token sequence, 64/8 heads, hd 128, fp16
     KV split into contiguous chunks across the ranks; each step = partial
-    (m, l, o) over the local chunk + NCCL all-gather + merge (strong scaling:
-    the total KV is fixed). Returns (ms per step, KV bytes of this rank)."""
+    (m, l, o) over the local chunk + the NVLink peer exchange fused with the
+    merge (strong scaling: the total KV is fixed). Returns (ms per step, KV bytes of this rank)."""
     from aspida_b200 import shard
     nq, nkv, hd, L = 64, 8, 128, 131072
     lo, hi = shard.kv_chunks(L, world)[rank]
@@ -220,6 +220,7 @@ def long_leg(ab, torch, dev, rank, world, steps, warmup, stream, dist):
         step()
     e1.record(stream)
     torch.cuda.synchronize()
+    op.close()
     return e0.elapsed_time(e1) / steps, n * nkv * hd * 2 * 2
 
 

@@ -219,6 +219,35 @@ int aspida_attn_merge_strided(const float* m, const float* l, const float* o, co
                               void* stream);
 
 /* ------------------------------------------------------------------------
+ * NVLink peer exchange for sequence-parallel decode, fused with the merge.
+ * No counterpart in the reference (it has no multi-GPU inference); it
+ * replaces an NCCL all-gather of the packed partials + aspida_attn_merge.
+ *   aspida_attn_peer_buffer_size(world, rows, hd): bytes of one rank's
+ *     receive buffer (two step-parity banks of `world` partial slots + flags).
+ *   aspida_attn_peer_alloc: cudaMalloc + zero-fill that many bytes and write
+ *     its 64-byte CUDA IPC handle (cudaIpcMemHandle_t) to ipc_handle.
+ *   aspida_attn_peer_open / _close: map / unmap another rank's buffer from
+ *     its handle (same node, peer access); _free releases one's own.
+ *   aspida_attn_exchange_merge: `part` = this rank's packed partial
+ *     [m[rows] | l[rows] | o[rows][hd]] (f32, 16-byte aligned, m in natural
+ *     log units as aspida_attn_decode_partial writes it); recv = host array
+ *     [world] of every rank's buffer as mapped in this process (recv[rank] =
+ *     its own); step = 1, 2, 3, ... identical on every rank. Sends `part` to
+ *     every rank over NVLink, waits (bounded) for every rank's partial of
+ *     this step and writes the merged out[rows][hd] (x sigmoid(gate) if
+ *     given). All ranks must call it once per step, in the same order, one
+ *     rank per GPU. world <= 8. A rank that never arrives makes the wait run
+ *     out after seconds: the device status word is set. */
+size_t aspida_attn_peer_buffer_size(int world, int rows, int hd);
+int aspida_attn_peer_alloc(size_t bytes, void** ptr, void* ipc_handle);
+int aspida_attn_peer_open(const void* ipc_handle, void** peer_ptr);
+int aspida_attn_peer_close(void* peer_ptr);
+int aspida_attn_peer_free(void* ptr);
+int aspida_attn_exchange_merge(const float* part, void* const* recv, int world, int rank,
+                               unsigned long long step, const float* gate, float* out, int rows,
+                               int hd, void* stream);
+
+/* ------------------------------------------------------------------------
  * Causal prefill attention on the tcgen05 tensor cores.
  * Replaces aspida_ggml_fattn_prefill (gpu/fattn_ggml.cuh:109-141) and the
  * shim's own prefill kernels (gpu/gpu_matvec.cu:3309-3682).
