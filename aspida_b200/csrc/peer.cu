@@ -16,12 +16,13 @@
 //      flag[rank] = tag with a system-scope release;
 //   2. every block waits (bounded) until all of its own buffer's flags of
 //      this bank read `tag` (system-scope acquire), then merges its share of
-//      the rows from the `world` slots.
+//      the outputs (one per thread) from the `world` slots.
 // Two banks are enough: a rank writes bank (t mod 2) of step t + 2 only
 // after it has received every rank's step t + 1 partial, and each rank
 // sends that only after its own step-t merge has finished reading bank
 // (t mod 2). A wait that runs out (a rank that never arrives) sets the
 // device status word and leaves; nothing spins without a bound.
+#include <algorithm>
 #include <cstring>
 
 #include "common.cuh"
@@ -54,22 +55,24 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-__global__ void __launch_bounds__(512) exchange_merge_kernel(const PeerArgs a) {
+__global__ void __launch_bounds__(256) exchange_merge_kernel(const PeerArgs a) {
   const int bank = (int)(a.tag & 1);
-  const int p = blockIdx.x;                     // destination rank of this block's send
+  const int p = blockIdx.x;                     // blocks 0..world-1 also send to rank p
   // 1. send: this rank's partial -> slot `rank` of rank p's bank
-  {
+  if (p < a.world) {
     float* dst = a.recv[p] + bank * a.bank_floats + (long)a.rank * a.stride;
     const float4* s4 = reinterpret_cast<const float4*>(a.part);
     float4* d4 = reinterpret_cast<float4*>(dst);
     const long n4 = a.per / 4;
     for (long i = threadIdx.x; i < n4; i += blockDim.x) d4[i] = s4[i];
     for (long i = n4 * 4 + threadIdx.x; i < a.per; i += blockDim.x) dst[i] = a.part[i];
-    __threadfence_system();
+    // the barrier makes the block's stores observed by thread 0, whose
+    // system-scope fence + release store then publishes them (cumulativity)
     __syncthreads();
     if (threadIdx.x == 0) {
       unsigned long long* fl = reinterpret_cast<unsigned long long*>(a.recv[p] + a.flags_off) +
                                bank * kMaxWorld + a.rank;
+      __threadfence_system();
       st_release_sys(fl, a.tag);
     }
   }
@@ -95,25 +98,39 @@ __global__ void __launch_bounds__(512) exchange_merge_kernel(const PeerArgs a) {
       }
     }
   }
+  // thread 0's acquire synchronises with every sender's release; the barrier
+  // orders the other threads' reads after it
   __syncthreads();
   if (!ok) return;
-  for (int s = 0; s < a.world; ++s) (void)ld_acquire_sys(myfl + s);   // per-thread acquire
-  // 3. merge this block's rows (rows split over the world blocks)
+  // 3. merge: one output element per thread; the loads of the `world` slots
+  // are independent, so each thread waits about one L2 round trip
   const float* base = a.recv[a.rank] + bank * a.bank_floats;
-  const long rows = a.rows;
-  const long r0 = rows * p / a.world, r1 = rows * (p + 1) / a.world;
-  for (long e = r0 * a.hd + threadIdx.x; e < r1 * a.hd; e += blockDim.x) {
+  const long rows = a.rows, n = rows * a.hd;
+  for (long e = (long)blockIdx.x * blockDim.x + threadIdx.x; e < n;
+       e += (long)gridDim.x * blockDim.x) {
     const long r = e / a.hd;
+    float ms[kMaxWorld], ls[kMaxWorld], os[kMaxWorld];
+#pragma unroll
+    for (int s = 0; s < kMaxWorld; ++s) {
+      if (s < a.world) {
+        const float* sl = base + s * a.stride;      // written by rank s over NVLink: via L2
+        ms[s] = __ldcg(sl + r);
+        ls[s] = __ldcg(sl + rows + r);
+        os[s] = __ldcg(sl + 2 * rows + e);
+      }
+    }
     float M = -3.402823466e38f;
-    for (int s = 0; s < a.world; ++s) M = fmaxf(M, __ldcg(base + s * a.stride + r));
+#pragma unroll
+    for (int s = 0; s < kMaxWorld; ++s)
+      if (s < a.world) M = fmaxf(M, ms[s]);
     float acc = 0.f, L = 0.f;
-    for (int s = 0; s < a.world; ++s) {
-      const float* sl = base + s * a.stride;         // written by rank s over NVLink: read via L2
-      const float ms = __ldcg(sl + r);
-      if (ms < -3.0e38f) continue;                   // empty slice
-      const float w = expf(ms - M);
-      L += w * __ldcg(sl + rows + r);
-      acc += w * __ldcg(sl + 2 * rows + e);
+#pragma unroll
+    for (int s = 0; s < kMaxWorld; ++s) {
+      if (s < a.world && ms[s] >= -3.0e38f) {       // skip empty slices
+        const float w = expf(ms[s] - M);
+        L += w * ls[s];
+        acc += w * os[s];
+      }
     }
     float v = L > 0.f ? acc / L : 0.f;
     if (a.gate) v *= 1.f / (1.f + expf(-a.gate[e]));
@@ -199,7 +216,10 @@ extern "C" int aspida_attn_exchange_merge(const float* part, void* const* recv, 
   a.rows = rows;
   a.hd = hd;
   a.tag = step;
-  exchange_merge_kernel<<<world, 512, 0, (cudaStream_t)stream>>>(a);
+  // blocks: at least one per destination rank, enough for one thread per output
+  const long outs = (long)rows * hd;
+  const int blocks = (int)std::max<long>(world, std::min<long>((outs + 255) / 256, 1024));
+  exchange_merge_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
   ASPIDA_CHECK_LAUNCH();
   return 0;
 }
