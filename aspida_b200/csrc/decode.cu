@@ -673,14 +673,14 @@ decode_kernel(const DecodeParams p) {
 
 // Merge the pieces of each split (sequence, kv head) segment, one block per
 // query head: the log-sum-exp merge of gpu/fattn_sk.cu:84-97. The block's
-// warps take every NW-th piece (lanes over dims), then reduce through shared
-// memory. Launched as a programmatic dependent of decode_kernel: the block
+// NW warps (8, or 32 when few segments are cut into many pieces) take every
+// NW-th piece (lanes over dims), then reduce through shared memory. Launched as a programmatic dependent of decode_kernel: the block
 // is scheduled early and waits in griddepcontrol.wait until the decode grid
 // has finished and its writes are visible. Sequences with an empty key range
 // (no units) get zeros (mode 0) or an empty partial (mode 1) here.
-template <int HD>
-__global__ void __launch_bounds__(256) combine_kernel(const DecodeParams p) {
-  constexpr int NW = 8, PER = HD / 32;
+template <int HD, int NW>
+__global__ void __launch_bounds__(NW * 32) combine_kernel(const DecodeParams p) {
+  constexpr int PER = HD / 32;
   __shared__ float red_o[NW][HD];
   __shared__ float red_m[NW], red_l[NW];
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -820,7 +820,10 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
   // merges as soon as the decode grid completes
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.B, p.nkv, p.G);
-  cfg.blockDim = dim3(256);
+  // few segments for many CTAs (one long sequence): a segment has about
+  // nctas / segments pieces; past 16, give each query head's merge 32 warps
+  const bool wide = (long)p.B * p.ngroups * 16 < p.nctas;
+  cfg.blockDim = dim3(wide ? 1024 : 256);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -828,7 +831,9 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaError_t e = cudaLaunchKernelEx(&cfg, combine_kernel<HD>, p); e != cudaSuccess)
+  if (cudaError_t e = wide ? cudaLaunchKernelEx(&cfg, combine_kernel<HD, 32>, p)
+                            : cudaLaunchKernelEx(&cfg, combine_kernel<HD, 8>, p);
+      e != cudaSuccess)
     return record_status((int)e);
   return 0;
 }
