@@ -114,31 +114,41 @@ class PeerExchange:
         if self.world > 8:
             raise ValueError("the peer exchange supports up to 8 ranks")
         self.rows, self.hd, self.step = rows, hd, 0
+        # every rank takes part in the same collectives whatever fails
+        # locally, so a failure is seen by all ranks and none is left waiting
         nbytes = self._lib.aspida_attn_peer_buffer_size(self.world, rows, hd)
         own = C.c_void_p()
         handle = (C.c_char * 64)()
         rc = self._lib.aspida_attn_peer_alloc(nbytes, C.byref(own), handle)
-        if rc:
-            raise GPUError(rc, "peer_alloc")
-        self._own = own.value
+        self._own = own.value if rc == 0 else None
+        self._mapped = []
         handles = [None] * self.world
         try:
-            dist.all_gather_object(handles, bytes(handle), group=group)
+            dist.all_gather_object(handles, bytes(handle) if rc == 0 else None, group=group)
         except Exception as e:
-            self._lib.aspida_attn_peer_free(self._own)
+            self.close(barrier=False)
             raise ShardError(f"peer handle exchange failed: {e}") from e
-        ptrs, self._mapped = [], []
+        if any(h is None for h in handles):
+            self.close(barrier=False)
+            raise ShardError("peer buffer allocation failed on a rank")
+        ptrs, ok = [], True
         for r, h in enumerate(handles):
             if r == self.rank:
                 ptrs.append(self._own)
                 continue
             p = C.c_void_p()
-            rc = self._lib.aspida_attn_peer_open((C.c_char * 64).from_buffer_copy(h), C.byref(p))
-            if rc:
-                self.close()
-                raise GPUError(rc, "peer_open")
-            self._mapped.append(p.value)
-            ptrs.append(p.value)
+            if ok and self._lib.aspida_attn_peer_open((C.c_char * 64).from_buffer_copy(h),
+                                                      C.byref(p)) == 0:
+                self._mapped.append(p.value)
+                ptrs.append(p.value)
+            else:
+                ok = False
+        flag = torch.tensor([0 if ok else 1], dtype=torch.int32, device=torch.device(
+            "cuda", torch.cuda.current_device()))
+        dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+        if int(flag.item()) != 0:
+            self.close(barrier=False)
+            raise ShardError("peer buffer mapping failed on a rank (no peer access?)")
         self.table = (C.c_void_p * self.world)(*ptrs)
 
     def __call__(self, part: torch.Tensor, out: torch.Tensor, gate: Optional[torch.Tensor] = None,
@@ -153,22 +163,22 @@ class PeerExchange:
             raise GPUError(rc, "exchange_merge")
         return out
 
-    def close(self):
+    def close(self, barrier: bool = True):
         """Unmap the peers' buffers and free this rank's (after a barrier, so
         no rank still stores into it)."""
         import torch.distributed as dist
-        if getattr(self, "_own", None) is None:
-            return
         torch.cuda.synchronize()
-        try:
-            dist.barrier(group=self.group)
-        except Exception:
-            pass
-        for p in self._mapped:
+        if barrier:
+            try:
+                dist.barrier(group=self.group)
+            except Exception:
+                pass
+        for p in getattr(self, "_mapped", []):
             self._lib.aspida_attn_peer_close(p)
         self._mapped = []
-        self._lib.aspida_attn_peer_free(self._own)
-        self._own = None
+        if getattr(self, "_own", None) is not None:
+            self._lib.aspida_attn_peer_free(self._own)
+            self._own = None
 
 
 class SeqParallelDecode:
