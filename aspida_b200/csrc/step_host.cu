@@ -35,6 +35,7 @@ struct Staging {
   size_t dev_bytes = 0;
   void* pinned = nullptr;    // lane descriptors, host side
   size_t pinned_bytes = 0;
+  bool pending = false;      // copies from `pinned` may still be in flight
 };
 
 std::mutex g_stage_mu;
@@ -90,8 +91,12 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
     s.pinned_bytes = desc_bytes;
   }
   // The pinned descriptor block is reused by the next call on this stream:
-  // finish the previous call's H2D before overwriting it.
-  cudaStreamSynchronize(st);
+  // a call that returned early may have left its H2D in flight (a complete
+  // call ends with a synchronisation, so there is nothing to wait for).
+  if (s.pending) {
+    cudaStreamSynchronize(st);
+    s.pending = false;
+  }
 
   unsigned char* hp = static_cast<unsigned char*>(s.pinned);
   __half** hK = reinterpret_cast<__half**>(hp);
@@ -114,6 +119,7 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
 
   const size_t qbytes = (size_t)B * nq * hd * sizeof(float), kbytes = (size_t)B * kvd * sizeof(float);
   int rc = 0;
+  s.pending = true;
   if ((rc = cuda_status(cudaMemcpyAsync(d, hp, desc_bytes, cudaMemcpyHostToDevice, st)))) return rc;
   if ((rc = cuda_status(cudaMemcpyAsync(dq, q, qbytes, cudaMemcpyHostToDevice, st)))) return rc;
   if ((rc = cuda_status(cudaMemcpyAsync(dk, k, kbytes, cudaMemcpyHostToDevice, st)))) return rc;
@@ -126,5 +132,7 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
                    scale, window, softcap, max_kv, 0, dws, ws, st)))
     return rc;
   if ((rc = cuda_status(cudaMemcpyAsync(out, dout, qbytes, cudaMemcpyDeviceToHost, st)))) return rc;
-  return cuda_status(cudaStreamSynchronize(st));
+  rc = cuda_status(cudaStreamSynchronize(st));
+  if (rc == 0) s.pending = false;
+  return rc;
 }
