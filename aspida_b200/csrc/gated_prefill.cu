@@ -6,7 +6,9 @@
 // zeroes `out` (fattn_ggml.cuh:117-122) so no stale attention is consumed.
 //
 // The queries are rounded to fp16 for the tensor cores by a small conversion
-// kernel into scratch kept per (device, stream) and grown on demand.
+// kernel into scratch kept per (device, stream) and grown on demand. When a
+// short chunk after a long prefix would leave SMs idle (hd 256), the same
+// scratch holds split-KV partials (prefill_split_plan).
 #include <map>
 #include <mutex>
 #include <utility>
@@ -19,7 +21,10 @@ namespace aspida {
 int prefill_batch(int nseq, const void* const* q, const void* const* K, const void* const* V,
                   const float* const* gate, void* const* out, const int* P, const int* pos_start,
                   int out_f32, int nq, int nkv, int hd, float scale, int window, float softcap,
-                  cudaStream_t st, const int* block_table, int num_blocks, int block_size);
+                  cudaStream_t st, const int* block_table, int num_blocks, int block_size,
+                  int nsplit, float* part);
+int prefill_split_plan(int P, int pos_start, int nq, int hd, int window);
+size_t prefill_split_bytes(int nsplit, int P, int nq, int hd);
 
 namespace {
 
@@ -50,18 +55,22 @@ extern "C" int aspida_attn_prefill_gated(const float* q_all, const void* K, cons
     rc = record_status(ASPIDA_ERR_ARG);
   } else {
     void* qh = nullptr;
+    float* part = nullptr;
+    const int nsplit = prefill_split_plan(P, pos_start, nq, hd, 0);
+    const size_t qbytes = ((size_t)n * 2 + 255) / 256 * 256;
     {
       int dev = 0;
       cudaGetDevice(&dev);
       std::lock_guard<std::mutex> lk(g_mu);
       auto& s = g_scratch[{dev, st}];
-      const size_t need = (size_t)n * 2;
+      const size_t need = qbytes + prefill_split_bytes(nsplit, P, nq, hd);
       if (s.second < need) {
         if (s.first) { cudaStreamSynchronize(st); cudaFree(s.first); s = {nullptr, 0}; }
         if (cudaMalloc(&s.first, need) != cudaSuccess) rc = record_status(ASPIDA_ERR_NOMEM);
         else s.second = need;
       }
       qh = s.first;
+      if (nsplit > 1 && qh) part = reinterpret_cast<float*>(static_cast<char*>(qh) + qbytes);
     }
     if (!rc) {
       const long n4 = n / 4;
@@ -74,7 +83,8 @@ extern "C" int aspida_attn_prefill_gated(const float* q_all, const void* K, cons
       const void* qv = qh;
       void* ov = out;
       rc = prefill_batch(1, &qv, &K, &V, gate ? &gate : nullptr, &ov, &P, &pos_start, 1, nq,
-                         nkv, hd, 1.0f / sqrtf((float)hd), 0, 0.0f, st, nullptr, 0, 0);
+                         nkv, hd, 1.0f / sqrtf((float)hd), 0, 0.0f, st, nullptr, 0, 0,
+                         nsplit, part);
     }
   }
   if (rc) cudaMemsetAsync(out, 0, (size_t)n * sizeof(float), st);  // never leave `out` stale

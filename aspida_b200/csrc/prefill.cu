@@ -64,6 +64,12 @@ struct PrefillParams {
   int pos_start[kMaxSeq];
   const int* btab[kMaxSeq];         // paged caches: block table per sequence, else null
   int block_size;                   // rows per block (a multiple of the key-tile height)
+  // split-KV (hd-256 kernel, one sequence, f32 output): each query tile's key
+  // range is cut into nsplit contiguous chunks, each an item writing an
+  // unnormalised partial; split_merge_kernel combines them
+  int nsplit;                       // 1 = no split
+  float* part_o;                    // [nsplit][P][nq][hd] unnormalised O
+  float* part_ml;                   // [nsplit][P][nq][2]: row max (log2 units), row sum
   DeviceStatus* status;
   int nq, nkv, G, window, out_f32, ntq;
   float scale_log2, softcap;
@@ -695,13 +701,24 @@ __device__ __forceinline__ bool wait1(uint64_t* bar, uint32_t parity, Sync1& sy,
 }
 
 struct Item1 {
-  int seq, h, qt, P, len, kvh, qf, x0, x1, n;
+  int seq, h, qt, P, len, kvh, qf, x0, x1, n, sp;
   bool valid;
 };
+
+// Key-tile chunk [a, b) of split sp of a query tile whose keys span tiles
+// [x0, x1): equal contiguous chunks; empty when a >= b.
+__host__ __device__ __forceinline__ void split_range(int x0, int x1, int nsplit, int sp, int& a,
+                                                     int& b) {
+  const int chunk = (x1 - x0 + nsplit - 1) / nsplit;
+  a = x0 + sp * chunk;
+  b = min(x1, a + chunk);
+}
 
 template <int BN>
 __device__ __forceinline__ Item1 make_item1(const PrefillParams& p, int nseq, int w) {
   Item1 it;
+  it.sp = w % p.nsplit;                    // the splits of one tile are dealt side by side
+  w /= p.nsplit;
   const int per = nseq * p.nq;
   it.qt = p.ntq - 1 - w / per;
   const int rem = w % per;
@@ -720,7 +737,14 @@ __device__ __forceinline__ Item1 make_item1(const PrefillParams& p, int nseq, in
   const int lo = p.window > 0 ? max(0, it.qf - p.window + 1) : 0;
   it.x0 = lo / BN;
   it.x1 = ql / BN + 1;
+  if (p.nsplit > 1) {
+    int a, b;
+    split_range(it.x0, it.x1, p.nsplit, it.sp, a, b);
+    it.x0 = a;
+    it.x1 = max(a, b);
+  }
   it.n = it.valid ? it.x1 - it.x0 : 0;
+  it.valid = it.valid && it.n > 0;
   return it;
 }
 
@@ -966,6 +990,30 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
         if (s == it.seq) { gt = p.gate[s]; outp = p.out[s]; }
       const long obase = ((long)row * p.nq + it.h) * HD + half * HO;
       const bool leader = sw == 0 && lane == 0;
+      if (p.nsplit > 1) {
+        // split-KV partial: unnormalised O and (m, l) relative to m_run
+        const long pr = ((long)it.sp * it.P + row) * p.nq + it.h;
+#pragma unroll 1
+        for (int c = 0; c < HO / 32; ++c) {
+          float o[32];
+          tc::tmem_ld32(ob + c * 32, o);
+          tc::tmem_wait_ld();
+          if (row < it.P) {
+            float4* dst = reinterpret_cast<float4*>(p.part_o + pr * HD + half * HO + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) dst[i] = make_float4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+          }
+        }
+        if (row < it.P && half == 0) {
+          p.part_ml[pr * 2] = m_run;
+          p.part_ml[pr * 2 + 1] = l_tot;
+        }
+        tc::fence_before_sync();
+        mbar_arrive(&sy.o_free);
+        if (leader) mbar_arrive(&sy.q_free);
+        ++ne;
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < HO / 32; ++c) {
         float o[32];
@@ -1020,6 +1068,41 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
   }
 }
 
+// Combines the split-KV partials of one sequence: per (row, head), the
+// log-sum-exp merge of gpu/fattn_sk.cu:84-97 over the splits that held keys
+// of the row's query tile (recomputed as make_item1 cut them), then
+// x sigmoid(gate). Block (row, head), one thread per dim.
+__global__ void split_merge_kernel(const PrefillParams p, int hd, int bn) {
+  const int row = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int P = p.P[0], ps = p.pos_start[0];
+  const int qt = row / BM, qf = ps + qt * BM;
+  const int ql = min(ps + P, qf + BM) - 1;
+  const int lo = p.window > 0 ? max(0, qf - p.window + 1) : 0;
+  const int x0 = lo / bn, x1 = ql / bn + 1;
+  float M = -INFINITY;
+  for (int s = 0; s < p.nsplit; ++s) {
+    int a, b;
+    split_range(x0, x1, p.nsplit, s, a, b);
+    if (a < b) M = fmaxf(M, p.part_ml[(((long)s * P + row) * p.nq + h) * 2]);
+  }
+  float L = 0.f, acc = 0.f;
+  for (int s = 0; s < p.nsplit; ++s) {
+    int a, b;
+    split_range(x0, x1, p.nsplit, s, a, b);
+    if (a >= b) continue;
+    const long pr = ((long)s * P + row) * p.nq + h;
+    const float m = p.part_ml[pr * 2];
+    if (m == -INFINITY) continue;                 // no key of this split reached the row
+    const float w = fast_exp2(m - M);
+    L += w * p.part_ml[pr * 2 + 1];
+    acc += w * p.part_o[pr * hd + d];
+  }
+  const long oi = ((long)row * p.nq + h) * hd + d;
+  float v = L > 0.f ? acc / L : 0.f;
+  if (p.gate[0]) v *= 1.f / (1.f + expf(-p.gate[0][oi]));
+  static_cast<float*>(p.out[0])[oi] = v;
+}
+
 template <int HD>
 int launch_prefill1(PrefillParams& p, int nseq, cudaStream_t st) {
   using Geo = PGeo1<HD>;
@@ -1032,10 +1115,14 @@ int launch_prefill1(PrefillParams& p, int nseq, cudaStream_t st) {
     if (e != cudaSuccess) return record_status((int)e);
     configured[dev] = true;
   }
-  const int nitems = p.ntq * p.nq * nseq;
+  const int nitems = p.ntq * p.nq * nseq * p.nsplit;
   const int grid = std::min(nitems, num_sms());
   prefill1_kernel<HD><<<grid, kThreads1, Geo::SMEM, st>>>(p, nseq, nitems);
   ASPIDA_CHECK_LAUNCH();
+  if (p.nsplit > 1) {
+    split_merge_kernel<<<dim3(p.P[0], p.nq), HD, 0, st>>>(p, HD, Geo::BN);
+    ASPIDA_CHECK_LAUNCH();
+  }
   return 0;
 }
 
@@ -1090,13 +1177,30 @@ int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
 
 }  // namespace
 
+// Split-KV plan for a single-sequence hd-256 prefill: when the (query tile,
+// head) items would leave SMs idle, cut each tile's key range into up to
+// SMs / items chunks of at least 4 key tiles (so a long prefix fills the
+// GPU); 1 = no split. prefill_split_bytes: the f32 partials' size.
+int prefill_split_plan(int P, int pos_start, int nq, int hd, int window) {
+  if (hd != 256 || P <= 0 || nq <= 0) return 1;
+  const int items = ((P + BM - 1) / BM) * nq;
+  const int sms = num_sms();
+  if (items * 2 > sms) return 1;
+  const int keys = window > 0 ? std::min(window + BM, pos_start + P) : pos_start + P;
+  const int ns = std::min(sms / items, std::max(1, keys / 64 / 4));
+  return std::max(1, std::min(ns, 16));
+}
+size_t prefill_split_bytes(int nsplit, int P, int nq, int hd) {
+  return nsplit > 1 ? (size_t)nsplit * P * nq * (hd + 2) * sizeof(float) : 0;
+}
+
 // Paged form (block_table != null, one sequence): K/V are pools of num_blocks
 // blocks of block_size rows.
 int prefill_batch(int nseq, const void* const* q, const void* const* K, const void* const* V,
                   const float* const* gate, void* const* out, const int* P, const int* pos_start,
                   int out_f32, int nq, int nkv, int hd, float scale, int window, float softcap,
                   cudaStream_t st, const int* block_table = nullptr, int num_blocks = 0,
-                  int block_size = 0) {
+                  int block_size = 0, int nsplit = 1, float* part = nullptr) {
   if (nseq <= 0) return 0;
   if (!q || !K || !V || !out || !P || !pos_start || nq <= 0 || nkv <= 0 || nq % nkv)
     return record_status(ASPIDA_ERR_ARG);
@@ -1137,6 +1241,14 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     if (maxP == 0) continue;
     p.status = device_status_ptr();
     p.block_size = block_size;
+    p.nsplit = 1;
+    if (nsplit > 1) {
+      // split-KV partials (the hd-256 kernel, one sequence, f32 output)
+      if (hd != 256 || nseq != 1 || !out_f32 || !part) return record_status(ASPIDA_ERR_ARG);
+      p.nsplit = nsplit;
+      p.part_o = part;
+      p.part_ml = part + (size_t)nsplit * P[0] * nq * hd;
+    }
     p.nq = nq; p.nkv = nkv; p.G = nq / nkv;
     p.window = window; p.out_f32 = out_f32;
     p.scale_log2 = scale * kLog2e;

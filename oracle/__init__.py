@@ -146,6 +146,8 @@ def prefill(q, K, V, pos_start, nq, nkv, hd, *, gate=None, scale=None, window=0,
     if scale is None:
         scale = 1.0 / np.sqrt(np.float32(hd))
     ra = np.ascontiguousarray(rows, dtype=np.int32) if rows is not None else None
+    if ra is not None and ra.size and (ra.min() < 0 or ra.max() >= P):
+        raise ValueError("rows must lie in [0, P)")
     threads = threads or os.cpu_count() or 1
     load().oracle_prefill(_p(q), _p(g), _p(K), _p(V), _p(out), P, pos_start, nq, nkv, hd,
                           float(scale), window, softcap, _p(ra), 0 if ra is None else ra.size,

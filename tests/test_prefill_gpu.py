@@ -118,3 +118,30 @@ def test_gated_prefill_exact_signature_hura_dims(ab, oracle):
     torch.cuda.synchronize()
     assert rc == ab.ASPIDA_ERR_UNSUPPORTED and float(bad.abs().max()) == 0.0
     ab.last_error()
+
+
+@pytest.mark.parametrize("P,ps", [(512, 8192), (100, 5000), (130, 1000)])
+def test_gated_prefill_split_kv(ab, oracle, P, ps):
+    """Short chunks after a long prefix at the hura dims: too few (query tile,
+    head) items for the SMs, so the key range of each tile is split over CTAs
+    and the partials merged (2, 9 and 4 splits here); sampled rows against
+    the oracle, including the partial last tile and rows whose causal range
+    ends inside a split."""
+    from aspida_b200 import _lib
+    nq, nkv, hd = 16, 2, 256
+    g = torch.Generator(device="cuda").manual_seed(P + ps)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda")
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    gate = torch.randn(P, nq * hd, generator=g, device="cuda")
+    out = torch.full((P, nq * hd), float("nan"), device="cuda")
+    rc = _lib.load().aspida_attn_prefill_gated(q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                               gate.data_ptr(), out.data_ptr(), nq, nkv, hd, P,
+                                               ps, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    rows = sorted(r for r in {0, 1, 63, 64, 127, 128, P // 2, P - 2, P - 1} if 0 <= r < P)
+    ref = oracle.prefill(q.cpu().numpy(), K.float().cpu().numpy(), V.float().cpu().numpy(), ps,
+                         nq, nkv, hd, gate=gate.cpu().numpy(), rows=rows)
+    assert_parity(out.cpu().numpy()[rows], ref[rows], what=f"split gated P={P} ps={ps}")
