@@ -31,6 +31,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <map>
 #include <mutex>
 
 #include "common.cuh"
@@ -64,7 +65,7 @@ struct PrefillParams {
   int pos_start[kMaxSeq];
   const int* btab[kMaxSeq];         // paged caches: block table per sequence, else null
   int block_size;                   // rows per block (a multiple of the key-tile height)
-  // split-KV (hd-256 kernel, one sequence, f32 output): each query tile's key
+  // split-KV (hd-256 kernel, one sequence): each query tile's key
   // range is cut into nsplit contiguous chunks, each an item writing an
   // unnormalised partial; split_merge_kernel combines them
   int nsplit;                       // 1 = no split
@@ -1100,7 +1101,8 @@ __global__ void split_merge_kernel(const PrefillParams p, int hd, int bn) {
   const long oi = ((long)row * p.nq + h) * hd + d;
   float v = L > 0.f ? acc / L : 0.f;
   if (p.gate[0]) v *= 1.f / (1.f + expf(-p.gate[0][oi]));
-  static_cast<float*>(p.out[0])[oi] = v;
+  if (p.out_f32) static_cast<float*>(p.out[0])[oi] = v;
+  else static_cast<__half*>(p.out[0])[oi] = __float2half_rn(v);
 }
 
 template <int HD>
@@ -1243,8 +1245,8 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     p.block_size = block_size;
     p.nsplit = 1;
     if (nsplit > 1) {
-      // split-KV partials (the hd-256 kernel, one sequence, f32 output)
-      if (hd != 256 || nseq != 1 || !out_f32 || !part) return record_status(ASPIDA_ERR_ARG);
+      // split-KV partials (the hd-256 kernel, one sequence)
+      if (hd != 256 || nseq != 1 || !part) return record_status(ASPIDA_ERR_ARG);
       p.nsplit = nsplit;
       p.part_o = part;
       p.part_ml = part + (size_t)nsplit * P[0] * nq * hd;
@@ -1268,13 +1270,43 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
 
 }  // namespace aspida
 
+namespace aspida {
+namespace {
+// Split-KV partial scratch of the single-sequence entry, per (device, stream).
+std::mutex g_split_mu;
+std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_split_scratch;
+}  // namespace
+
+// Scratch of at least `bytes` for split partials on (current device, st), or
+// null when it cannot be had (the caller then runs without splitting).
+float* split_scratch(size_t bytes, cudaStream_t st) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_split_mu);
+  auto& s = g_split_scratch[{dev, st}];
+  if (s.second < bytes) {
+    if (s.first) { cudaStreamSynchronize(st); cudaFree(s.first); s = {nullptr, 0}; }
+    if (cudaMalloc(&s.first, bytes) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+    s.second = bytes;
+  }
+  return static_cast<float*>(s.first);
+}
+}  // namespace aspida
+
 extern "C" int aspida_attn_prefill(const void* q, const void* K, const void* V, const float* gate,
                                    void* out, int out_f32, int nq, int nkv, int hd, int P,
                                    int pos_start, float scale, int window, float softcap,
                                    void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  int nsplit = aspida::prefill_split_plan(P, pos_start, nq, hd, window);
+  float* part = nullptr;
+  if (nsplit > 1) {
+    part = aspida::split_scratch(aspida::prefill_split_bytes(nsplit, P, nq, hd), st);
+    if (!part) nsplit = 1;
+  }
   return aspida::prefill_batch(1, &q, &K, &V, gate ? &gate : nullptr, &out, &P, &pos_start,
-                               out_f32, nq, nkv, hd, scale, window, softcap,
-                               (cudaStream_t)stream);
+                               out_f32, nq, nkv, hd, scale, window, softcap, st, nullptr, 0, 0,
+                               nsplit, part);
 }
 
 extern "C" int aspida_attn_prefill_paged(const void* q, const void* K_pool, const void* V_pool,

@@ -257,7 +257,10 @@ int aspida_attn_exchange_merge(const float* part, void* const* recv, int world, 
  *   out    dev [P][nq*hd], fp16 (out_f32 = 0) or f32 (out_f32 = 1)
  *   query t (position pos_start+t) attends keys max(0, pos-window+1)..pos;
  *   scale / window / softcap as for decode.
- * All pointers 16-byte aligned. Supported: hd in {64, 128, 256}. */
+ * All pointers 16-byte aligned. Supported: hd in {64, 128, 256}.
+ * At hd 256, a chunk whose (query tile, head) items cannot fill the GPU has
+ * each tile's key range split over CTAs; the partials live in library
+ * scratch kept per (device, stream), allocated on first need. */
 int aspida_attn_prefill(const void* q, const void* K, const void* V, const float* gate, void* out,
                         int out_f32, int nq, int nkv, int hd, int P, int pos_start, float scale,
                         int window, float softcap, void* stream);

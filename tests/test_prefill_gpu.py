@@ -145,3 +145,23 @@ def test_gated_prefill_split_kv(ab, oracle, P, ps):
     ref = oracle.prefill(q.cpu().numpy(), K.float().cpu().numpy(), V.float().cpu().numpy(), ps,
                          nq, nkv, hd, gate=gate.cpu().numpy(), rows=rows)
     assert_parity(out.cpu().numpy()[rows], ref[rows], what=f"split gated P={P} ps={ps}")
+
+
+@pytest.mark.parametrize("window", [0, 1024])
+def test_prefill_hd256_short_chunk_split_fp16(ab, oracle, window):
+    """aspida_attn_prefill at hd 256 with a short chunk after a long prefix
+    (Gemma-style: softcap 50, scale 1/16, fp16 output): the split-KV path with
+    library scratch and an fp16 merge; sampled rows against the oracle."""
+    nq, nkv, hd, P, ps = 16, 8, 256, 200, 6000
+    g = torch.Generator(device="cuda").manual_seed(window + 7)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda").half()
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    out = ab.prefill(q, K, V, nq, nkv, hd, ps, scale=1.0 / 16, window=window, softcap=50.0)
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    rows = [0, 1, 100, 127, 128, 198, 199]
+    ref = oracle.prefill(q.float().cpu().numpy(), K.float().cpu().numpy(),
+                         V.float().cpu().numpy(), ps, nq, nkv, hd, rows=rows, scale=1.0 / 16,
+                         window=window, softcap=50.0)
+    assert_parity(out.float().cpu().numpy()[rows], ref[rows], what=f"split fp16 window={window}")
