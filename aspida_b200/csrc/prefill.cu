@@ -65,7 +65,7 @@ struct PrefillParams {
   int pos_start[kMaxSeq];
   const int* btab[kMaxSeq];         // paged caches: block table per sequence, else null
   int block_size;                   // rows per block (a multiple of the key-tile height)
-  // split-KV (hd-256 kernel, one sequence): each query tile's key
+  // split-KV (one-tile kernel, one sequence): each query tile's key
   // range is cut into nsplit contiguous chunks, each an item writing an
   // unnormalised partial; split_merge_kernel combines them
   int nsplit;                       // 1 = no split
@@ -1179,12 +1179,13 @@ int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
 
 }  // namespace
 
-// Split-KV plan for a single-sequence hd-256 prefill: when the (query tile,
-// head) items would leave SMs idle, cut each tile's key range into up to
-// SMs / items chunks of at least 4 key tiles (so a long prefix fills the
-// GPU); 1 = no split. prefill_split_bytes: the f32 partials' size.
+// Split-KV plan for a single-sequence prefill on the one-tile kernel (hd 256,
+// or hd 128 for short chunks): when its (128-row query tile, head) items
+// would leave SMs idle, cut each tile's key range into up to SMs / items
+// chunks of at least 4 key tiles (so a long prefix fills the GPU); 1 = no
+// split. prefill_split_bytes: the f32 partials' size.
 int prefill_split_plan(int P, int pos_start, int nq, int hd, int window) {
-  if (hd != 256 || P <= 0 || nq <= 0) return 1;
+  if ((hd != 256 && hd != 128) || P <= 0 || nq <= 0) return 1;
   const int items = ((P + BM - 1) / BM) * nq;
   const int sms = num_sms();
   if (items * 2 > sms) return 1;
@@ -1218,7 +1219,15 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     PrefillParams p;
     memset(&p, 0, sizeof(p));
     int maxP = 0;
-    const int box_kv = hd <= 128 ? 128 : 64;
+    for (int i = 0; i < cnt; ++i) maxP = std::max(maxP, P[base + i]);
+    // hd 128 normally runs two 128-row query tiles per item; a chunk too
+    // short to fill the SMs with such items (or one being split) runs one
+    // tile per item on the 64-key one-tile kernel instead
+    const bool one_tile =
+        hd == 256 || (hd == 128 && (nsplit > 1 || (long)((maxP + 2 * BM - 1) / (2 * BM)) * nq *
+                                                          cnt * 2 <= num_sms()));
+    const int box_kv = one_tile ? 64 : 128;           // the kernel's key-tile height
+    maxP = 0;
     for (int i = 0; i < cnt; ++i) {
       const int s = base + i;
       if (P[s] < 0 || pos_start[s] < 0 || !q[s] || !K[s] || !V[s] || !out[s])
@@ -1245,8 +1254,8 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     p.block_size = block_size;
     p.nsplit = 1;
     if (nsplit > 1) {
-      // split-KV partials (the hd-256 kernel, one sequence)
-      if (hd != 256 || nseq != 1 || !part) return record_status(ASPIDA_ERR_ARG);
+      // split-KV partials (the one-tile kernel, one sequence)
+      if (!one_tile || nseq != 1 || !part) return record_status(ASPIDA_ERR_ARG);
       p.nsplit = nsplit;
       p.part_o = part;
       p.part_ml = part + (size_t)nsplit * P[0] * nq * hd;
@@ -1256,12 +1265,12 @@ int prefill_batch(int nseq, const void* const* q, const void* const* K, const vo
     p.scale_log2 = scale * kLog2e;
     p.softcap = softcap;
     int rc;
-    if (hd <= 128) {
+    if (!one_tile) {
       p.ntq = (maxP + 2 * BM - 1) / (2 * BM);          // 256-row tiles
       rc = hd == 64 ? launch_prefill2<64>(p, cnt, st) : launch_prefill2<128>(p, cnt, st);
     } else {
       p.ntq = (maxP + BM - 1) / BM;
-      rc = launch_prefill1<256>(p, cnt, st);
+      rc = hd == 128 ? launch_prefill1<128>(p, cnt, st) : launch_prefill1<256>(p, cnt, st);
     }
     if (rc) return rc;
   }

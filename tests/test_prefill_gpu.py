@@ -165,3 +165,23 @@ def test_prefill_hd256_short_chunk_split_fp16(ab, oracle, window):
                          V.float().cpu().numpy(), ps, nq, nkv, hd, rows=rows, scale=1.0 / 16,
                          window=window, softcap=50.0)
     assert_parity(out.float().cpu().numpy()[rows], ref[rows], what=f"split fp16 window={window}")
+
+
+@pytest.mark.parametrize("P,ps,out_dtype", [(300, 0, torch.float16), (100, 5000, torch.float32),
+                                            (100, 5000, torch.float16)])
+def test_prefill_hd128_short_chunk_one_tile(ab, oracle, P, ps, out_dtype):
+    """hd 128 chunks too short to fill the SMs with two-tile items run on the
+    one-tile kernel (P=300: no split; P=100 after 5000 keys: 4 splits);
+    sampled rows against the oracle."""
+    nq, nkv, hd = 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(P + ps + 3)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda").half()
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    out = ab.prefill(q, K, V, nq, nkv, hd, ps, out_dtype=out_dtype)
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    rows = sorted(r for r in {0, 1, 63, 64, 127, 128, P // 2, P - 2, P - 1} if 0 <= r < P)
+    ref = oracle.prefill(q.float().cpu().numpy(), K.float().cpu().numpy(),
+                         V.float().cpu().numpy(), ps, nq, nkv, hd, rows=rows)
+    assert_parity(out.float().cpu().numpy()[rows], ref[rows], what=f"hd128 one-tile P={P}")
