@@ -311,6 +311,22 @@ def decode_q8(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor, Ks_tab:
     return out
 
 
+def prefill_q8_gated(q: torch.Tensor, K8: torch.Tensor, V8: torch.Tensor, Ks: torch.Tensor,
+                     Vs: torch.Tensor, nq: int, nkv: int, hd: int, pos_start: int = 0, *,
+                     gate: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                     stream=None) -> torch.Tensor:
+    """Gated causal prefill over Q8_0 caches (k_gqa_kv<..., 2> semantics):
+    q f32 [P, nq*hd]; K8/V8 int8 [rows, nkv*hd]; Ks/Vs fp16 [rows, nkv*hd/32]."""
+    P = q.shape[0]
+    if out is None:
+        out = torch.empty((P, nq * hd), dtype=torch.float32, device=q.device)
+    rc = _lib_().aspida_attn_prefill_q8_gated(
+        _ptr(q), _ptr(gate), _ptr(K8), _ptr(V8), _ptr(Ks), _ptr(Vs), _ptr(out), nq, nkv, hd, P,
+        pos_start, _stream(stream))
+    _check(rc, "prefill_q8_gated")
+    return out
+
+
 def decode_partial(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor,
                    kv_lo: torch.Tensor, kv_hi: torch.Tensor, nq: int, nkv: int, hd: int, *,
                    scale: Optional[float] = None, softcap: float = 0.0, max_kv_len: int,

@@ -195,6 +195,19 @@ int aspida_attn_decode_q8(const float* q, const float* gate, const void* const* 
                           float softcap, int max_kv_len, int chunk, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* Gated causal prefill over Q8_0 caches with the argument meaning of the
+ * reference's k_gqa_kv<..., 2> (gpu/fattn_kvhalf.cu:59-130, launched at
+ * 162-190): q_all / gate f32 [P][nq*hd] (q 16-byte aligned), K8 / V8 int8
+ * caches and K_scales / V_scales fp16 scales (Q8_0 layout, >= pos_start+P
+ * rows), out f32 [P][nq*hd]; query t at position pos_start+t attends keys
+ * 0..pos_start+t, scale 1/sqrt(hd), out *= sigmoid(gate). The cache prefix
+ * is dequantised into per-stream fp16 scratch (int8 x scale, rounded to fp16)
+ * and the tcgen05 prefill runs on it. Zeroes `out` on failure. */
+int aspida_attn_prefill_q8_gated(const float* q_all, const float* gate, const void* K8,
+                                 const void* V8, const void* K_scales, const void* V_scales,
+                                 float* out, int nq, int nkv, int hd, int P, int pos_start,
+                                 void* stream);
+
 /* Q8_0 quantiser, the algorithm of k_to_q8 (gpu/fattn_kvhalf.cu:143-152):
  * nblk blocks of 32 consecutive f32 values; scales[b] = fp16(max|v|/127),
  * q = clamp(round-to-nearest-even(v * (1/d)), -127, 127), zeros for an

@@ -155,3 +155,41 @@ def test_decode_q8_unsupported_and_errors(ab):
     assert e.value.code == -4
     with pytest.raises(ValueError):
         ab.quantize_q8(torch.zeros(33, device="cuda"))
+
+
+@pytest.mark.parametrize("c", cases.Q8_GQA_CASES, ids=lambda c: c["name"])
+def test_prefill_q8_gated_matches_reference_kernel(ab, c):
+    """aspida_attn_prefill_q8_gated on the golden cases: the reference's own
+    k_to_q8 + k_gqa_kv<2, hd/32, 2> outputs (gated causal chunks over a Q8_0
+    cache); our quantiser is bit-exact, so the caches are the same."""
+    p = os.path.join(GOLDEN, c["name"] + ".npz")
+    if not os.path.exists(p):
+        pytest.skip("golden fixture missing")
+    ref = np.load(p)["out"].reshape(c["P"], -1)
+    q, g, K, V = cases.q8_gqa_inputs(c)
+    kq, ks = ab.quantize_q8(torch.from_numpy(K).cuda())
+    vq, vs = ab.quantize_q8(torch.from_numpy(V).cuda())
+    got = ab.prefill_q8_gated(torch.from_numpy(q).cuda(), kq, vq, ks, vs, c["nq"], c["nkv"],
+                              c["hd"], c["ps"], gate=torch.from_numpy(g).cuda())
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    assert_parity(got.cpu().numpy(), ref, what=f"q8 prefill vs reference {c['name']}")
+
+
+def test_prefill_q8_gated_hura_vs_oracle(ab, oracle):
+    """A 300-token chunk after 2000 keys at the hura dims (16/2 heads, hd 256)
+    against the oracle on the dequantised caches (sampled rows)."""
+    nq, nkv, hd, P, ps = 16, 2, 256, 300, 2000
+    g = torch.Generator(device="cuda").manual_seed(12)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda")
+    gate = torch.randn(P, nq * hd, generator=g, device="cuda")
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda")
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda")
+    kq, ks = ab.quantize_q8(K)
+    vq, vs = ab.quantize_q8(V)
+    got = ab.prefill_q8_gated(q, kq, vq, ks, vs, nq, nkv, hd, ps, gate=gate)
+    torch.cuda.synchronize()
+    rows = [0, 1, 127, 128, 200, 298, 299]
+    ref = oracle.prefill(q.cpu().numpy(), deq(oracle, kq, ks), deq(oracle, vq, vs), ps, nq, nkv,
+                         hd, gate=gate.cpu().numpy(), rows=rows)
+    assert_parity(got.cpu().numpy()[rows], ref[rows], what="q8 prefill hura")
