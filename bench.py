@@ -332,10 +332,21 @@ def cfg4_legs(ab, torch, dev, steps, warmup, stream, seed):
             ab.decode(qd, Kt, Vt, pos, nq, nkv, hd, scale=sc, softcap=cap, window=W,
                       max_kv_len=L, out=od, workspace=ws, stream=stream)
 
-    d_ms = _time(torch, stream, decode_step, steps, warmup)
+    d_ms_eager = _time(torch, stream, decode_step, steps, warmup)
+    # the same 6-layer step captured once in a CUDA graph and replayed: the
+    # window layers read 67 MB each, so per-call host overhead would show
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        cs = torch.cuda.current_stream()
+        for layer in range(6):
+            ab.decode(qd, Kt, Vt, pos, nq, nkv, hd, scale=sc, softcap=cap,
+                      window=0 if layer == 0 else W, max_kv_len=L, out=od, workspace=ws,
+                      stream=cs)
+    torch.cuda.synchronize()
+    d_ms = _time(torch, stream, graph.replay, steps, warmup)
     d_bytes = B * nkv * hd * 2 * 2 * (L + 5 * W) + 6 * B * nq * hd * 8
     return {"prefill_ms": p_ms, "prefill_flops": p_flops, "decode_ms": d_ms,
-            "decode_bytes": d_bytes}
+            "decode_ms_eager": d_ms_eager, "decode_bytes": d_bytes}
 
 
 def cfg5b_leg(ab, torch, dev, steps, warmup, stream, seed):
@@ -655,7 +666,8 @@ def main():
                         "frac_of_tensor_peak": round(c4["prefill_flops"] / (c4["prefill_ms"] * 1e-3)
                                                      / 1e12 / tc_peak, 4)},
             "decode": {"value": round(c4d_all / (c4d_max * 1e-3) / 1e9, 1), "unit": "GB/s",
-                       "ms_per_step": round(c4d_max, 4),
+                       "ms_per_step": round(c4d_max, 4), "cuda_graph": True,
+                       "ms_per_step_eager": round(c4["decode_ms_eager"], 4),
                        "frac_of_hbm": round(c4["decode_bytes"] / (c4["decode_ms"] * 1e-3) / 1e9
                                             / hbm_peak, 4)},
             "gpu_launches": x_steps * 6 * 3,
