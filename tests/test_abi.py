@@ -4,6 +4,8 @@ import ctypes
 import os
 import re
 
+import pytest
+
 from aspida_b200 import _lib
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -37,3 +39,28 @@ def test_workspace_size_is_host_only_and_monotone():
     c = lib.aspida_attn_decode_workspace_size(64, 32, 8, 128, 8192, 512)
     assert 0 < a <= b and a < c
     assert lib.aspida_attn_decode_workspace_size(0, 32, 8, 128, 8192, 512) == 0
+
+
+@pytest.mark.gpu
+def test_c_program_drives_the_library_like_the_ada_binding(tmp_path):
+    """tests/c/abi_decode.c: dlopen + dlsym of the entry points, a KV state
+    from the lifecycle calls, one batched decode, checked in C against a
+    double-precision CPU loop (no Python in the data path)."""
+    import shutil
+    import subprocess
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    exe = tmp_path / "abi_decode"
+    subprocess.run([gcc, "-O2", "-o", str(exe), os.path.join(ROOT, "tests", "c", "abi_decode.c"),
+                    f"-I{cuda}/include", f"-L{cuda}/lib64", "-lcudart", "-ldl", "-lm"],
+                   check=True, timeout=120)
+    env = dict(os.environ, LD_LIBRARY_PATH=f"{cuda}/lib64:" + os.environ.get("LD_LIBRARY_PATH", ""))
+    r = subprocess.run([str(exe), _lib.LIB_PATH], capture_output=True, text=True, timeout=120,
+                       env=env)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert r.stdout.startswith("max_abs")
