@@ -42,6 +42,9 @@ SIGNATURES = {
                                        f32, i32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_decode_partial": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32,
                                          f32, f32, i32, i32, vp, sz, vp]),
+    "aspida_attn_decode_fused": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp,
+                                       vp, f32, i32, f32, f32, f32, i32, f32, f32, vp, i32, i32,
+                                       i32, f32, i32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_decode_q8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
                                     i32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_quantize_q8": (i32, [vp, vp, vp, C.c_longlong, vp]),

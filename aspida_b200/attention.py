@@ -327,6 +327,34 @@ def prefill_q8_gated(q: torch.Tensor, K8: torch.Tensor, V8: torch.Tensor, Ks: to
     return out
 
 
+def decode_fused(q_raw: torch.Tensor, k_raw: torch.Tensor, v_raw: torch.Tensor,
+                 K_tab: torch.Tensor, V_tab: torch.Tensor, pos: torch.Tensor, nq: int, nkv: int,
+                 hd: int, rope: RopeParams, *, q_norm: Optional[torch.Tensor] = None,
+                 k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6,
+                 gate: Optional[torch.Tensor] = None, max_len: Optional[torch.Tensor] = None,
+                 scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
+                 max_kv_len: int, chunk: int = 0, out: Optional[torch.Tensor] = None,
+                 workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """prep + decode in one launch: raw queries and the new raw K/V rows
+    [B, nkv*hd] (appended at pos into the fp16 caches of the tables)."""
+    B = q_raw.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((B, nq * hd), dtype=torch.float32, device=q_raw.device)
+    nbytes = decode_workspace_size(B, nq, nkv, hd, max_kv_len, chunk)
+    wsb = _ws(workspace, q_raw.device).get(nbytes, q_raw.device)
+    ff = rope.freq_factors if rope.use_ff else None
+    rc = _lib_().aspida_attn_decode_fused(
+        _ptr(q_raw), _ptr(k_raw), _ptr(v_raw), _ptr(gate), _ptr(K_tab), _ptr(V_tab), _ptr(pos),
+        _ptr(max_len), _ptr(out), B, nq, nkv, hd, _ptr(q_norm), _ptr(k_norm), eps, rope.dim,
+        rope.freq_base, rope.freq_scale, rope.m_scale, int(rope.yarn_on), rope.corr_low,
+        rope.corr_high, _ptr(ff), int(rope.use_ff), int(rope.interleaved), rope.sec_total,
+        scale, window, softcap, max_kv_len, chunk, _ptr(wsb), wsb.numel(), _stream(stream))
+    _check(rc, "decode_fused")
+    return out
+
+
 def decode_partial(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor,
                    kv_lo: torch.Tensor, kv_hi: torch.Tensor, nq: int, nkv: int, hd: int, *,
                    scale: Optional[float] = None, softcap: float = 0.0, max_kv_len: int,

@@ -122,6 +122,27 @@ __device__ __forceinline__ void mma_16816(float* d, const uint32_t* a, uint32_t 
 }
 
 // 8x8 b16 transpose across the warp (fragment layout: row lane/4, cols 2*(lane%4)+{0,1}).
+// RoPE angle of pair i at position pos_eff (LLM_RoPE.Apply_Sections,
+// src/llm/llm_rope.adb:84-200, and k_fattn_prep, gpu/gpu_matvec.cu:1449-1503):
+// theta = pos/base^(2i/rd), x freq_scale or the YaRN blend, / ff[i]. Shared
+// by the prep kernel and the fused decode so both rotate identically.
+__device__ __forceinline__ float rope_angle(int i, int pos_eff, int rd, float base,
+                                            float freq_scale, int yarn_on, float corr_lo,
+                                            float corr_hi, const float* ff, int use_ff) {
+  float extrap = (float)pos_eff / powf(base, (float)(2 * i) / (float)rd);
+  float th;
+  if (yarn_on) {
+    float interp = freq_scale * extrap;
+    float y = ((float)i - corr_lo) / fmaxf(0.001f, corr_hi - corr_lo);
+    float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
+    th = interp * (1.0f - ramp) + extrap * ramp;
+  } else {
+    th = extrap * freq_scale;
+  }
+  if (use_ff) th = th / ff[i];
+  return th;
+}
+
 __device__ __forceinline__ uint32_t lds_u32(uint32_t saddr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));

@@ -78,6 +78,17 @@ struct DecodeParams {
   float* ws_ml;         // [slots][HPC][8][2]  (m in log2 units, l)
   float* ws_o;          // [slots][HPC][8][hd]
   DeviceStatus* status;
+  // fused pre-attention step (aspida_attn_decode_fused): `q` holds raw
+  // queries; the new raw K/V rows are appended at pos by the CTA that owns
+  // each sequence's last unit; QK-RMSNorm weights (or null) and RoPE
+  // parameters as for aspida_attn_prep
+  const float* k_new;
+  const float* v_new;
+  const float* q_norm;
+  const float* k_norm;
+  const float* ff;
+  float eps, rbase, freq_scale, m_scale, corr_lo, corr_hi;
+  int fuse, rd, yarn_on, use_ff, interleaved, sec_total;
   long slots;
   int B, nq, nkv, G, window, mode;
   int hpc, ngroups;     // kv heads per CTA, head groups
@@ -229,7 +240,186 @@ __device__ __forceinline__ int out_dim(int mt, int j, int g) {
   else return mt * 16 + g + (j >> 1) * 8;
 }
 
-template <int HD, int HPC, bool Q8>
+// Fused step, at a piece's start: RMSNorm (optional) and RoPE of this lane's
+// raw query values (fp16 fragment layout: qv[kt][j] = dim kt*16 + qc + off,
+// off = 0, 1, 8, 9). The 4 lanes of a column hold all its dims; a NeoX pair
+// (d, d + rd/2) sits in one lane (kt and kt + rd/32) because rd is a multiple
+// of 32, an interleaved pair (2i, 2i+1) in j = 0/1 or 2/3. Same formulas as
+// prep_kernel (sum of squares reduced across the 4 lanes).
+template <int HD>
+__device__ __forceinline__ void fuse_q(const DecodeParams& p, float (&qv)[HD / 16][4], int pos,
+                                       int qc, int lane) {
+  constexpr int KT = HD / 16, NA = HD / 64;     // angles per lane: pairs lane + 32k, k < NA
+  if (p.q_norm) {
+    float ss = 0.f;
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ss = fmaf(qv[kt][j], qv[kt][j], ss);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    const float rms = sqrtf(ss / (float)HD + p.eps);
+#pragma unroll
+    for (int kt = 0; kt < KT; ++kt)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d = kt * 16 + qc + (j & 1) + (j >> 1) * 8;
+        qv[kt][j] = __fmul_rn(qv[kt][j] / rms, p.q_norm[d]);
+      }
+  }
+  // every angle once per warp: lane l evaluates pairs l + 32k (the same
+  // formula as prep_kernel); a pair's lane fetches its cos / sin by shuffle
+  const int npair = p.rd / 2;
+  float ca[NA], sa[NA];
+#pragma unroll
+  for (int k = 0; k < NA; ++k) {
+    const int i = lane + 32 * k;
+    ca[k] = 1.f;
+    sa[k] = 0.f;
+    if (i < npair) {
+      const int pos_eff = i < p.sec_total ? pos : 0;
+      const float th = rope_angle(i, pos_eff, p.rd, p.rbase, p.freq_scale, p.yarn_on, p.corr_lo,
+                                  p.corr_hi, p.ff, p.use_ff);
+      ca[k] = __fmul_rn(cosf(th), p.m_scale);
+      sa[k] = __fmul_rn(sinf(th), p.m_scale);
+    }
+  }
+  const int half = p.rd / 2;
+#pragma unroll
+  for (int kt = 0; kt < KT; ++kt) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int d = kt * 16 + qc + (j & 1) + (j >> 1) * 8;
+      // pair index of this dim (as the first of its pair), or -1
+      int i = -1, kt2 = kt, j2 = j;
+      if (p.interleaved) {
+        if (d < p.rd && !(d & 1)) { i = d >> 1; j2 = j + 1; }
+      } else if (d < half) {
+        i = d;
+        kt2 = kt + half / 16;
+      }
+      // all lanes take part in the shuffles; i's owner lane is i & 31
+      const int src = i < 0 ? 0 : (i & 31), k = i < 0 ? 0 : (i >> 5);
+      float c = 0.f, sn = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < NA; ++kk) {
+        const float cv = __shfl_sync(0xffffffffu, ca[kk], src);
+        const float sv = __shfl_sync(0xffffffffu, sa[kk], src);
+        if (kk == k) { c = cv; sn = sv; }
+      }
+      if (i < 0) continue;
+      float x2 = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk)                 // kt2 is not a compile-time index
+        if (kk == kt2) x2 = qv[kk][j2];
+      const float x1 = qv[kt][j];
+      const float o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+      const float o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+      qv[kt][j] = o1;
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk)
+        if (kk == kt2) qv[kk][j2] = o2;
+    }
+  }
+}
+
+// One warp appends sequence b's new row for kv head kvh at position pos:
+// V as given, K RMSNorm'ed (optional) and rotated, both to fp16 - the
+// arithmetic of prep_kernel, in the same order (sequential sum of squares,
+// the same angle function), so the cache rows are identical. sh: HD floats
+// of scratch for the warp.
+template <int HD>
+__device__ void append_row(const DecodeParams& p, int b, int kvh, int pos, float* sh, int lane) {
+  const long kvd = (long)p.nkv * HD;
+  const float* kr = p.k_new + (long)b * kvd + (long)kvh * HD;
+  const float* vr = p.v_new + (long)b * kvd + (long)kvh * HD;
+  __half* Kc = const_cast<__half*>(p.K[b]) + (long)pos * kvd + (long)kvh * HD;
+  __half* Vc = const_cast<__half*>(p.V[b]) + (long)pos * kvd + (long)kvh * HD;
+  for (int d = lane; d < HD; d += 32) {
+    Vc[d] = __float2half_rn(vr[d]);
+    sh[d] = kr[d];
+  }
+  __syncwarp();
+  float rms = 1.f;
+  if (p.k_norm) {
+    float ss = 0.f;
+    if (lane == 0)
+      for (int i = 0; i < HD; ++i) ss = __fadd_rn(ss, __fmul_rn(sh[i], sh[i]));
+    ss = __shfl_sync(0xffffffffu, ss, 0);
+    rms = sqrtf(ss / (float)HD + p.eps);
+  }
+  float nv[HD / 32];
+#pragma unroll
+  for (int j = 0; j < HD / 32; ++j) {
+    const int d = lane + 32 * j;
+    nv[j] = p.k_norm ? __fmul_rn(sh[d] / rms, p.k_norm[d]) : sh[d];
+  }
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < HD / 32; ++j) sh[lane + 32 * j] = nv[j];
+  __syncwarp();
+#pragma unroll
+  for (int j = 0; j < HD / 32; ++j) {
+    const int d = lane + 32 * j;
+    float o = nv[j];
+    if (d < p.rd) {
+      const int half = p.rd / 2;
+      int i, other;
+      bool first;
+      if (p.interleaved) {
+        i = d >> 1;
+        first = (d & 1) == 0;
+        other = first ? d + 1 : d - 1;
+      } else if (d < half) {
+        i = d;
+        first = true;
+        other = d + half;
+      } else {
+        i = d - half;
+        first = false;
+        other = d - half;
+      }
+      const int pos_eff = i < p.sec_total ? pos : 0;
+      const float th = rope_angle(i, pos_eff, p.rd, p.rbase, p.freq_scale, p.yarn_on, p.corr_lo,
+                                  p.corr_hi, p.ff, p.use_ff);
+      const float c = __fmul_rn(cosf(th), p.m_scale), sn = __fmul_rn(sinf(th), p.m_scale);
+      const float x1 = first ? nv[j] : sh[other];
+      const float x2 = first ? sh[other] : nv[j];
+      o = first ? __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn))
+                : __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+    }
+    Kc[d] = __float2half_rn(o);
+  }
+  __syncwarp();
+}
+
+// Fused step: this CTA appends the new row of every (sequence, head group)
+// segment whose last unit lies in its range [u0, u1) - the only unit that
+// reads row pos - one consumer warp per kv head of the group.
+template <int HD, int HPC>
+__device__ void append_owned_rows(const DecodeParams& p, const int* pref, long u0, long u1,
+                                  float* scratch, int warp, int lane) {
+  long u = u0;
+  while (u < u1) {
+    int lo = 0, hi = p.B;                 // largest b with pref[b] <= u
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pref[mid] <= u) lo = mid; else hi = mid;
+    }
+    const int b = lo;
+    int klo, khi;
+    seq_range(p, b, klo, khi);
+    const int nu = (khi - klo + kKeys - 1) / kKeys;
+    const int grp = (int)((u - pref[b]) / nu);
+    const long s1 = pref[b] + (long)(grp + 1) * nu;
+    const int pos = p.pos[b];
+    if (s1 - 1 < u1 && pos >= 0 && khi == pos + 1 && warp < HPC)
+      append_row<HD>(p, b, grp * HPC + warp, pos, scratch + warp * HD, lane);
+    u = s1;
+  }
+}
+
+template <int HD, int HPC, bool Q8, bool FUSE = false>
 __global__ void __launch_bounds__(Geometry<HD, HPC, Q8>::THREADS, 1)
 decode_kernel(const DecodeParams p) {
   using Geo = Geometry<HD, HPC, Q8>;
@@ -262,6 +452,17 @@ decode_kernel(const DecodeParams p) {
   const long cta = blockIdx.x;
   if (cta >= C) return;
   const long u_begin = range_start(cta, U, C), u_end = range_start(cta + 1, U, C);
+  if constexpr (FUSE) {
+    {
+      // append the new rows this CTA will read, before its producer starts
+      // (the stage buffers are idle scratch until then); the async-proxy
+      // fence orders these generic stores before the bulk copies
+      append_owned_rows<HD, HPC>(p, pref, u_begin, u_end, reinterpret_cast<float*>(smem), warp,
+                                 lane);
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      __syncthreads();
+    }
+  }
   Cursor cur;
   cur.u = u_begin;
   cur.u_end = u_end;
@@ -385,22 +586,29 @@ decode_kernel(const DecodeParams p) {
       // first unit of a piece: this kv head's G query rows as an fp16 hi/lo
       // pair in B-fragment layout; reset the softmax state
       const float* qb = p.q + ((long)cur.b * p.nq + (long)kvh * p.G) * HD;
+      // this lane's query values of column g: qv[kt][j] = dims kt*16 + off(j),
+      // fp16 path off = qc, qc+1, qc+8, qc+9; Q8 path 2qc .. 2qc+3
+      float qv[KT][4];
 #pragma unroll
       for (int kt = 0; kt < KT; ++kt) {
-        // fp16 path: B rows k (2t, 2t+1 | 2t+8, 2t+9) are dims (qc, qc+1 |
-        // qc+8, qc+9) of the step; Q8 path: dims (4t, 4t+1 | 4t+2, 4t+3)
-        float2 a = make_float2(0.f, 0.f), c = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) qv[kt][j] = 0.f;
         if (g < p.G) {
           if constexpr (Q8) {
             const float4 f = *reinterpret_cast<const float4*>(qb + g * HD + kt * 16 + 2 * qc);
-            a = make_float2(f.x, f.y);
-            c = make_float2(f.z, f.w);
+            qv[kt][0] = f.x; qv[kt][1] = f.y; qv[kt][2] = f.z; qv[kt][3] = f.w;
           } else {
             const int d = kt * 16 + qc;
-            a = *reinterpret_cast<const float2*>(qb + g * HD + d);
-            c = *reinterpret_cast<const float2*>(qb + g * HD + d + 8);
+            const float2 a = *reinterpret_cast<const float2*>(qb + g * HD + d);
+            const float2 c = *reinterpret_cast<const float2*>(qb + g * HD + d + 8);
+            qv[kt][0] = a.x; qv[kt][1] = a.y; qv[kt][2] = c.x; qv[kt][3] = c.y;
           }
         }
+      }
+      if constexpr (FUSE) fuse_q<HD>(p, qv, p.pos[cur.b], qc, lane);
+#pragma unroll
+      for (int kt = 0; kt < KT; ++kt) {
+        const float2 a = make_float2(qv[kt][0], qv[kt][1]), c = make_float2(qv[kt][2], qv[kt][3]);
         const __half2 ah = __floats2half2_rn(a.x, a.y), ch = __floats2half2_rn(c.x, c.y);
         const float2 ar = __half22float2(ah), cr = __half22float2(ch);
         qhi[kt][0] = *reinterpret_cast<const uint32_t*>(&ah);
@@ -794,11 +1002,11 @@ WsLayout ws_layout(int B, int nkv, int hd, int hpc) {
   return w;
 }
 
-template <int HD, int HPC, bool Q8>
+template <int HD, int HPC, bool Q8, bool FUSE = false>
 int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st) {
   using Geo = Geometry<HD, HPC, Q8>;
   const size_t smem = (size_t)Geo::STAGES * Geo::STAGE_BYTES + (size_t)(p.B + 1) * sizeof(int);
-  auto kern = decode_kernel<HD, HPC, Q8>;
+  auto kern = decode_kernel<HD, HPC, Q8, FUSE>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -848,6 +1056,14 @@ int launch_decode_hd(DecodeParams& p, long units_hint, int chunk, cudaStream_t s
       case 4: return launch_decode_v<HD, 4, true>(p, units_hint, chunk, st);
       case 2: return launch_decode_v<HD, (HD >= 128 ? 2 : 4), true>(p, units_hint, chunk, st);
       default: return launch_decode_v<HD, (HD == 256 ? 1 : 4), true>(p, units_hint, chunk, st);
+    }
+  }
+  if (p.fuse) {
+    switch (heads_per_cta(p.nkv, HD)) {
+      case 8: return launch_decode_v<HD, (HD <= 128 ? 8 : 4), false, true>(p, units_hint, chunk, st);
+      case 4: return launch_decode_v<HD, 4, false, true>(p, units_hint, chunk, st);
+      case 2: return launch_decode_v<HD, 2, false, true>(p, units_hint, chunk, st);
+      default: return launch_decode_v<HD, 1, false, true>(p, units_hint, chunk, st);
     }
   }
   switch (heads_per_cta(p.nkv, HD)) {
@@ -971,6 +1187,35 @@ int decode_partial(const float* q, const void* const* K, const void* const* V, c
   return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
 }
 
+int decode_fused(const float* q_raw, const float* k_raw, const float* v_raw, const float* gate,
+                 const void* const* K, const void* const* V, const int* pos, const int* max_len,
+                 float* out, int B, int nq, int nkv, int hd, const float* q_norm,
+                 const float* k_norm, float eps, int rd, float base, float freq_scale,
+                 float m_scale, int yarn_on, float corr_lo, float corr_hi, const float* ff,
+                 int use_ff, int interleaved, int sec_total, float scale, int window,
+                 float softcap, int max_kv_len, int chunk, void* ws, size_t ws_bytes,
+                 cudaStream_t st) {
+  DecodeParams p{};
+  p.q = q_raw; p.gate = gate;
+  p.K = reinterpret_cast<const __half* const*>(K);
+  p.V = reinterpret_cast<const __half* const*>(V);
+  p.pos = pos; p.max_len = max_len; p.out = out;
+  p.B = B; p.nq = nq; p.nkv = nkv; p.G = nkv > 0 ? nq / nkv : 0;
+  p.window = window; p.mode = 0;
+  p.scale_log2 = scale * kLog2e; p.softcap = softcap;
+  p.fuse = 1;
+  p.k_new = k_raw; p.v_new = v_raw; p.q_norm = q_norm; p.k_norm = k_norm; p.eps = eps;
+  p.rd = rd; p.rbase = base; p.freq_scale = freq_scale; p.m_scale = m_scale;
+  p.yarn_on = yarn_on; p.corr_lo = corr_lo; p.corr_hi = corr_hi; p.ff = ff; p.use_ff = use_ff;
+  p.interleaved = interleaved; p.sec_total = sec_total;
+  if (B > 0 && (!pos || !out || !k_raw || !v_raw || rd < 0 || rd > hd || (rd & 1) ||
+                (use_ff && !ff)))
+    return record_status(ASPIDA_ERR_ARG);
+  // a NeoX pair (d, d + rd/2) must sit in one lane of the fragment layout
+  if (!interleaved && (rd % 32) != 0) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  return run_decode(p, hd, max_kv_len, chunk, ws, ws_bytes, st);
+}
+
 int decode_q8(const float* q, const float* gate, const void* const* K8, const void* const* V8,
               const void* const* Ks, const void* const* Vs, const int* pos, const int* max_len,
               float* out, int B, int nq, int nkv, int hd, float scale, int window, float softcap,
@@ -1050,6 +1295,21 @@ extern "C" int aspida_attn_decode_q8(const float* q, const float* gate, const vo
   return aspida::decode_q8(q, gate, K8, V8, K_scales, V_scales, pos, max_len, out, B, nq, nkv,
                            hd, scale, window, softcap, max_kv_len, chunk, workspace,
                            workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_decode_fused(
+    const float* q_raw, const float* k_raw, const float* v_raw, const float* gate,
+    const void* const* K, const void* const* V, const int* pos, const int* max_len, float* out,
+    int B, int nq, int nkv, int hd, const float* q_norm, const float* k_norm, float eps, int rd,
+    float base, float freq_scale, float m_scale, int yarn_on, float corr_lo, float corr_hi,
+    const float* ff, int use_ff, int interleaved, int sec_total, float scale, int window,
+    float softcap, int max_kv_len, int chunk, void* workspace, size_t workspace_bytes,
+    void* stream) {
+  return aspida::decode_fused(q_raw, k_raw, v_raw, gate, K, V, pos, max_len, out, B, nq, nkv, hd,
+                              q_norm, k_norm, eps, rd, base, freq_scale, m_scale, yarn_on,
+                              corr_lo, corr_hi, ff, use_ff, interleaved, sec_total, scale, window,
+                              softcap, max_kv_len, chunk, workspace, workspace_bytes,
+                              (cudaStream_t)stream);
 }
 
 extern "C" int aspida_attn_quantize_q8(const float* in, void* q, void* scales, long long nblk,

@@ -12,23 +12,6 @@
 namespace aspida {
 namespace {
 
-__device__ __forceinline__ float rope_angle(int i, int pos_eff, int rd, float base,
-                                            float freq_scale, int yarn_on, float corr_lo,
-                                            float corr_hi, const float* ff, int use_ff) {
-  float extrap = (float)pos_eff / powf(base, (float)(2 * i) / (float)rd);
-  float th;
-  if (yarn_on) {
-    float interp = freq_scale * extrap;
-    float y = ((float)i - corr_lo) / fmaxf(0.001f, corr_hi - corr_lo);
-    float ramp = 1.0f - fminf(1.0f, fmaxf(0.0f, y));
-    th = interp * (1.0f - ramp) + extrap * ramp;
-  } else {
-    th = extrap * freq_scale;
-  }
-  if (use_ff) th = th / ff[i];
-  return th;
-}
-
 // grid (P, nq + nkv), block hd. Block (t, h<nq) handles query head h of token
 // t; block (t, nq + j) handles kv head j (K rotated, V copied).
 __global__ void prep_kernel(const float* __restrict__ q, const float* __restrict__ k,

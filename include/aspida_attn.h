@@ -180,6 +180,30 @@ int aspida_attn_decode_partial(const float* q, const void* const* K, const void*
                                int max_kv_len, int chunk, void* workspace,
                                size_t workspace_bytes, void* stream);
 
+/* Decode fused with the pre-attention step (the row-per-sequence case of
+ * k_fattn_prep, gpu/gpu_matvec.cu:1449-1503, followed by the attention of
+ * k_fattn_attend_b): q_raw dev f32 [B][nq*hd] un-normed, un-rotated queries;
+ * k_raw, v_raw dev f32 [B][nkv*hd] the new token's key / value rows, appended
+ * at pos[b] (K RMSNorm'ed with k_norm if given and rotated, V as given, both
+ * fp16) unless pos[b] >= max_len[b]; queries RMSNorm'ed with q_norm if given
+ * and rotated in registers. RoPE parameters as for aspida_attn_prep (NeoX
+ * requires rd % 32 == 0, else ASPIDA_ERR_UNSUPPORTED); the cache rows written
+ * equal aspida_attn_prep's. Other arguments and the workspace as
+ * aspida_attn_decode (fp16 per-sequence caches). One launch replaces
+ * aspida_attn_prep + aspida_attn_decode; measured on B200 at config 2 it is
+ * slower than the two (0.137 vs ~0.107 ms): the rotation and the appends
+ * serialise on the bandwidth-bound kernel's critical path, where the prep
+ * kernel spreads them over the whole GPU. */
+int aspida_attn_decode_fused(const float* q_raw, const float* k_raw, const float* v_raw,
+                             const float* gate, const void* const* K, const void* const* V,
+                             const int* pos, const int* max_len, float* out, int B, int nq,
+                             int nkv, int hd, const float* q_norm, const float* k_norm, float eps,
+                             int rd, float base, float freq_scale, float m_scale, int yarn_on,
+                             float corr_lo, float corr_hi, const float* ff, int use_ff,
+                             int interleaved, int sec_total, float scale, int window,
+                             float softcap, int max_kv_len, int chunk, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Decode over Q8_0 KV caches: the storage of the reference's KVMODE 2
  * (k_gqa_kv<..., 2>, gpu/fattn_kvhalf.cu:55-130; tile-load dequant at 88-92):
  *   K8, V8          dev tables [B] of dev int8 caches [rows][nkv*hd]

@@ -182,8 +182,10 @@ def test_prep_rope_and_append(ab, oracle):
     cache.free()
 
 
-def test_step_host_matches_oracle(ab, oracle):
-    """Host-buffer step: RoPE'd K/V append at pos + decode, end to end."""
+@pytest.mark.parametrize("rd", [128, 48])
+def test_step_host_matches_oracle(ab, oracle, rd):
+    """Host-buffer step: RoPE'd K/V append at pos + decode, end to end
+    (full and partial rotary)."""
     nq, nkv, hd = 32, 8, 128
     lens = [77, 1000, 1]
     caches = [ab.KVCache(L + 8, nkv, hd, nq) for L in lens]
@@ -202,10 +204,11 @@ def test_step_host_matches_oracle(ab, oracle):
     v = torch.from_numpy(rng.standard_normal((B, nkv * hd)).astype(np.float32)).pin_memory()
     out = torch.empty(B, nq * hd).pin_memory()
     ab.step_host([c.handle for c in caches], q, k, v, lens, out, nq, nkv, hd,
-                 rope_dim=hd, rope_base=500000.0)
-    qr = np.stack([oracle.rope_rows(q[b:b + 1].numpy(), nq, hd, [lens[b]], 500000.0)[0] for b in range(B)])
+                 rope_dim=rd, rope_base=500000.0)
+    qr = np.stack([oracle.rope_rows(q[b:b + 1].numpy(), nq, hd, [lens[b]], 500000.0, rd=rd)[0]
+                   for b in range(B)])
     for b in range(B):
-        kr = oracle.rope_rows(k[b:b + 1].numpy(), nkv, hd, [lens[b]], 500000.0)[0]
+        kr = oracle.rope_rows(k[b:b + 1].numpy(), nkv, hd, [lens[b]], 500000.0, rd=rd)[0]
         Kf[b] = np.concatenate([Kf[b], kr.astype(np.float16).astype(np.float32)[None]])
         Vf[b] = np.concatenate([Vf[b], v[b:b + 1].numpy().astype(np.float16).astype(np.float32)])
     ref = oracle.decode_batch(qr, Kf, Vf, lens, nq, nkv, hd)
@@ -332,3 +335,58 @@ def test_decode_cuda_graph_replay(ab):
     torch.cuda.synchronize()
     assert torch.equal(out1, eager)
     assert ab.device_status() == 0
+
+
+@pytest.mark.parametrize("hd,nq,nkv,rd,inter,norm,sec", [
+    (128, 32, 8, 128, False, False, None), (128, 32, 8, 64, False, True, None),
+    (128, 16, 4, 128, True, True, None), (64, 8, 2, 64, False, False, 16),
+    (256, 16, 8, 256, False, True, None)])
+def test_decode_fused_matches_prep_then_decode(ab, oracle, hd, nq, nkv, rd, inter, norm, sec):
+    """aspida_attn_decode_fused (new rows appended by the owning CTA, queries
+    normed and rotated in registers) against aspida_attn_prep + decode on
+    copies of the same caches: appended rows bit-identical; outputs identical
+    without QK-norm (same arithmetic) and within 1e-5 with it (the query sum
+    of squares is reduced in another order); a clamped position appends
+    nothing."""
+    lens = [1, 17, 300, 1000]
+    B = len(lens)
+    q0, Ks, Vs = make_batch([L + 2 for L in lens], nq, nkv, hd, seed=hd + rd + int(inter))
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q_raw = torch.randn(B, nq * hd, generator=g, device="cuda")
+    k_raw = torch.randn(B, nkv * hd, generator=g, device="cuda")
+    v_raw = torch.randn(B, nkv * hd, generator=g, device="cuda")
+    gate = torch.randn(B, nq * hd, generator=g, device="cuda")
+    qn = (torch.rand(hd, generator=g, device="cuda") + 0.5) if norm else None
+    kn = (torch.rand(hd, generator=g, device="cuda") + 0.5) if norm else None
+    rope = ab.RopeParams(dim=rd, freq_base=500000.0, interleaved=inter,
+                         sections=() if sec is None else (sec, 0, 0, 0))
+    pos_l = [L - 1 for L in lens]
+    ml_l = [L + 2 for L in lens[:-1]] + [lens[-1] - 1]   # the last new position is clamped
+    pos = torch.tensor(pos_l, dtype=torch.int32, device="cuda")
+    ml = torch.tensor(ml_l, dtype=torch.int32, device="cuda")
+    K2, V2 = [k.clone() for k in Ks], [v.clone() for v in Vs]
+    # two-step reference path
+    qr = torch.empty_like(q_raw)
+    for b in range(B):
+        if pos_l[b] < ml_l[b]:
+            qr[b:b + 1] = ab.prep(q_raw[b:b + 1], k_raw[b:b + 1], v_raw[b:b + 1], K2[b], V2[b],
+                                  pos_l[b], nq, nkv, hd, rope, q_norm=qn, k_norm=kn)
+        else:   # prep would not append: rotate the query with a throwaway cache
+            Kt_, Vt_ = K2[b].clone(), V2[b].clone()
+            qr[b:b + 1] = ab.prep(q_raw[b:b + 1], k_raw[b:b + 1], v_raw[b:b + 1], Kt_, Vt_,
+                                  pos_l[b], nq, nkv, hd, rope, q_norm=qn, k_norm=kn)
+    ref = ab.decode(qr, ab.ptr_table(K2, q_raw.device), ab.ptr_table(V2, q_raw.device), pos, nq,
+                    nkv, hd, gate=gate, max_len=ml, window=200, max_kv_len=max(lens) + 2)
+    got = ab.decode_fused(q_raw, k_raw, v_raw, ab.ptr_table(Ks, q_raw.device),
+                          ab.ptr_table(Vs, q_raw.device), pos, nq, nkv, hd, rope, q_norm=qn,
+                          k_norm=kn, gate=gate, max_len=ml, window=200,
+                          max_kv_len=max(lens) + 2)
+    torch.cuda.synchronize()
+    assert ab.device_status() == 0
+    for b in range(B):
+        assert torch.equal(Ks[b], K2[b]), f"K cache of sequence {b}"
+        assert torch.equal(Vs[b], V2[b]), f"V cache of sequence {b}"
+    if norm:
+        assert float((got - ref).abs().max()) <= 1e-5
+    else:
+        assert torch.equal(got, ref)
