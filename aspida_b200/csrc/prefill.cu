@@ -33,6 +33,8 @@
 #include <cmath>
 #include <map>
 #include <mutex>
+#include <vector>
+#include <queue>
 
 #include "common.cuh"
 #include "tcgen05.cuh"
@@ -69,6 +71,9 @@ struct PrefillParams {
   // range is cut into nsplit contiguous chunks, each an item writing an
   // unnormalised partial; split_merge_kernel combines them
   int nsplit;                       // 1 = no split
+  // two-tile kernel: per-CTA item lists (CSR: offsets [grid + 1], then the
+  // items), balanced on the host; null = items dealt boustrophedon-wise
+  const int* sched;
   float* part_o;                    // [nsplit][P][nq][hd] unnormalised O
   float* part_ml;                   // [nsplit][P][nq][2]: row max (log2 units), row sum
   DeviceStatus* status;
@@ -333,7 +338,14 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
   // items are dealt boustrophedon-wise (round rr: CTA c takes the c-th item, or
   // the (C-1-c)-th on odd rounds) over the heaviest-first list, which evens out
   // the per-CTA load
+  // or, with a host schedule, taken from this CTA's list; every role walks
+  // the same sequence
+  const int* sch = p.sched;
+  const int s_begin = sch ? sch[blockIdx.x] : 0;
+  const int rounds = sch ? sch[blockIdx.x + 1] - s_begin
+                         : (nitems + (int)gridDim.x - 1) / (int)gridDim.x;
   auto snake_item = [&](int rr) {
+    if (sch) return sch[gridDim.x + 1 + s_begin + rr];
     const int c = (rr & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
     return rr * (int)gridDim.x + c;
   };
@@ -345,7 +357,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
       int qrel[2] = {0, 0};      // q_free arrivals expected so far per query tile
       bool pend[2] = {false, false};
       int ic = 0;        // items started
-      for (int rr = 0; rr * (int)gridDim.x < nitems && !sy.abort; ++rr) {
+      for (int rr = 0; rr < rounds && !sy.abort; ++rr) {
         const int w = snake_item(rr);
         if (w >= nitems) continue;
         const Item it = make_item<BN>(p, nseq, w);
@@ -417,7 +429,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
         }
       };
       bool ok = true;
-      for (int rr = 0; ok && rr * (int)gridDim.x < nitems; ++rr) {
+      for (int rr = 0; ok && rr < rounds; ++rr) {
         const int w = snake_item(rr);
         if (w >= nitems) continue;
         const Item it = make_item<BN>(p, nseq, w);
@@ -493,7 +505,7 @@ prefill2_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
     auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
     int ks = 0;                                       // S tiles consumed (all items)
     int ne = 0;                                       // epilogues done
-    for (int rr = 0; rr * (int)gridDim.x < nitems && !sy.abort; ++rr) {
+    for (int rr = 0; rr < rounds && !sy.abort; ++rr) {
         const int w = snake_item(rr);
         if (w >= nitems) continue;
       const Item it = make_item<BN>(p, nseq, w);
@@ -1158,6 +1170,73 @@ bool make_map(CUtensorMap* m, const void* base, long cols, long rows, int box_ro
   return r == CUDA_SUCCESS;
 }
 
+// Longest-processing-time-first schedule of the two-tile kernel's items over
+// `grid` CTAs: an item's cost is the key tiles of its two query tiles plus a
+// fixed 2 for its Q load and epilogues (the same tile ranges make_item
+// computes); items go, heaviest first, to the least-loaded CTA. Kept on the
+// device per (device, shape); null when it cannot be had (then the kernel
+// deals items boustrophedon-wise).
+const int* two_tile_schedule(const PrefillParams& p, int nseq, int nitems, int grid,
+                             cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;                       // no synchronous upload inside a capture
+  }
+  constexpr int BN = 128;
+  std::vector<int> key = {grid, nitems, nseq, p.nq, p.ntq, p.window};
+  for (int s = 0; s < nseq; ++s) { key.push_back(p.P[s]); key.push_back(p.pos_start[s]); }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  key.push_back(dev);
+  static std::mutex mu;
+  static std::map<std::vector<int>, int*> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if (auto f = cache.find(key); f != cache.end()) return f->second;
+  const int per = nseq * p.nq;
+  std::vector<std::pair<long, int>> cost(nitems);
+  for (int w = 0; w < nitems; ++w) {
+    const int qt = p.ntq - 1 - w / per, seq = (w % per) / p.nq;
+    const int P = p.P[seq], ps = p.pos_start[seq];
+    long c = 2;
+    for (int X = 0; X < 2; ++X) {
+      const int r0 = qt * 2 * BM + X * BM;
+      if (r0 >= P) continue;
+      const int qf = ps + r0, ql = std::min(ps + P, qf + BM) - 1;
+      const int lo = p.window > 0 ? std::max(0, qf - p.window + 1) : 0;
+      c += ql / BN + 1 - lo / BN;
+    }
+    cost[w] = {qt * 2 * BM < P ? c : 0, w};
+  }
+  std::stable_sort(cost.begin(), cost.end(),
+                   [](const auto& a, const auto& b) { return a.first > b.first; });
+  std::vector<std::vector<int>> lists(grid);
+  std::priority_queue<std::pair<long, int>, std::vector<std::pair<long, int>>,
+                      std::greater<std::pair<long, int>>> load;
+  for (int c = 0; c < grid; ++c) load.push({0, c});
+  for (const auto& [c, w] : cost) {
+    auto [l, cta] = load.top();
+    load.pop();
+    lists[cta].push_back(w);
+    load.push({l + c, cta});
+  }
+  std::vector<int> csr(grid + 1 + nitems);
+  csr[0] = 0;
+  for (int c = 0; c < grid; ++c) {
+    csr[c + 1] = csr[c] + (int)lists[c].size();
+    std::copy(lists[c].begin(), lists[c].end(), csr.begin() + grid + 1 + csr[c]);
+  }
+  int* d = nullptr;
+  if (cudaMalloc(&d, csr.size() * sizeof(int)) != cudaSuccess ||
+      cudaMemcpy(d, csr.data(), csr.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    if (d) cudaFree(d);
+    return nullptr;
+  }
+  cache[key] = d;
+  return d;
+}
+
 template <int HD>
 int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
   using Geo = PGeo2<HD>;
@@ -1172,6 +1251,7 @@ int launch_prefill2(PrefillParams& p, int nseq, cudaStream_t st) {
   }
   const int nitems = p.ntq * p.nq * nseq;
   const int grid = std::min(nitems, num_sms());
+  p.sched = nitems > grid ? two_tile_schedule(p, nseq, nitems, grid, st) : nullptr;
   prefill2_kernel<HD><<<grid, kThreads2, Geo::SMEM, st>>>(p, nseq, nitems);
   ASPIDA_CHECK_LAUNCH();
   return 0;
