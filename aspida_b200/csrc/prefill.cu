@@ -800,7 +800,12 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = sy.tmem_base;
+  const int* sch = p.sched;                  // host schedule, or boustrophedon dealing
+  const int s_begin = sch ? sch[blockIdx.x] : 0;
+  const int rounds = sch ? sch[blockIdx.x + 1] - s_begin
+                         : (nitems + (int)gridDim.x - 1) / (int)gridDim.x;
   auto snake_item = [&](int rr) {
+    if (sch) return sch[gridDim.x + 1 + s_begin + rr];
     const int c = (rr & 1) ? (int)gridDim.x - 1 - (int)blockIdx.x : (int)blockIdx.x;
     return rr * (int)gridDim.x + c;
   };
@@ -810,7 +815,7 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
     if (tc::elect_one()) {
       long g = 0;
       int ic = 0;
-      for (int rr = 0; rr * (int)gridDim.x < nitems && !sy.abort; ++rr) {
+      for (int rr = 0; rr < rounds && !sy.abort; ++rr) {
         const int w = snake_item(rr);
         if (w >= nitems) continue;
         const Item1 it = make_item1<BN>(p, nseq, w);
@@ -865,7 +870,7 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
         tc::commit(&sy.k_empty[s]);
         ++kS;
       };
-      for (int rr = 0; ok && rr * (int)gridDim.x < nitems; ++rr) {
+      for (int rr = 0; ok && rr < rounds; ++rr) {
         const int w = snake_item(rr);
         if (w >= nitems) continue;
         const Item1 it = make_item1<BN>(p, nseq, w);
@@ -917,7 +922,7 @@ prefill1_kernel(const __grid_constant__ PrefillParams p, int nseq, int nitems) {
     const float sc = capped ? 1.f : p.scale_log2;
     auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(bar_id) : "memory"); };
     int ks = 0, ne = 0;
-    for (int rr = 0; rr * (int)gridDim.x < nitems && !sy.abort; ++rr) {
+    for (int rr = 0; rr < rounds && !sy.abort; ++rr) {
       const int w = snake_item(rr);
       if (w >= nitems) continue;
       const Item1 it = make_item1<BN>(p, nseq, w);
@@ -1117,6 +1122,9 @@ __global__ void split_merge_kernel(const PrefillParams p, int hd, int bn) {
   else static_cast<__half*>(p.out[0])[oi] = __float2half_rn(v);
 }
 
+const int* one_tile_schedule(const PrefillParams& p, int nseq, int nitems, int grid,
+                             cudaStream_t st);
+
 template <int HD>
 int launch_prefill1(PrefillParams& p, int nseq, cudaStream_t st) {
   using Geo = PGeo1<HD>;
@@ -1131,6 +1139,7 @@ int launch_prefill1(PrefillParams& p, int nseq, cudaStream_t st) {
   }
   const int nitems = p.ntq * p.nq * nseq * p.nsplit;
   const int grid = std::min(nitems, num_sms());
+  p.sched = nitems > grid ? one_tile_schedule(p, nseq, nitems, grid, st) : nullptr;
   prefill1_kernel<HD><<<grid, kThreads1, Geo::SMEM, st>>>(p, nseq, nitems);
   ASPIDA_CHECK_LAUNCH();
   if (p.nsplit > 1) {
@@ -1207,6 +1216,75 @@ const int* two_tile_schedule(const PrefillParams& p, int nseq, int nitems, int g
       c += ql / BN + 1 - lo / BN;
     }
     cost[w] = {qt * 2 * BM < P ? c : 0, w};
+  }
+  std::stable_sort(cost.begin(), cost.end(),
+                   [](const auto& a, const auto& b) { return a.first > b.first; });
+  std::vector<std::vector<int>> lists(grid);
+  std::priority_queue<std::pair<long, int>, std::vector<std::pair<long, int>>,
+                      std::greater<std::pair<long, int>>> load;
+  for (int c = 0; c < grid; ++c) load.push({0, c});
+  for (const auto& [c, w] : cost) {
+    auto [l, cta] = load.top();
+    load.pop();
+    lists[cta].push_back(w);
+    load.push({l + c, cta});
+  }
+  std::vector<int> csr(grid + 1 + nitems);
+  csr[0] = 0;
+  for (int c = 0; c < grid; ++c) {
+    csr[c + 1] = csr[c] + (int)lists[c].size();
+    std::copy(lists[c].begin(), lists[c].end(), csr.begin() + grid + 1 + csr[c]);
+  }
+  int* d = nullptr;
+  if (cudaMalloc(&d, csr.size() * sizeof(int)) != cudaSuccess ||
+      cudaMemcpy(d, csr.data(), csr.size() * sizeof(int), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaGetLastError();
+    if (d) cudaFree(d);
+    return nullptr;
+  }
+  cache[key] = d;
+  return d;
+}
+
+// The same schedule for the one-tile kernel: an item (query tile, head,
+// split) costs its key tiles (64 keys) plus 2.
+const int* one_tile_schedule(const PrefillParams& p, int nseq, int nitems, int grid,
+                             cudaStream_t st) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  constexpr int BN = 64;
+  std::vector<int> key = {-1, grid, nitems, nseq, p.nq, p.ntq, p.window, p.nsplit};
+  for (int s = 0; s < nseq; ++s) { key.push_back(p.P[s]); key.push_back(p.pos_start[s]); }
+  int dev = 0;
+  cudaGetDevice(&dev);
+  key.push_back(dev);
+  static std::mutex mu;
+  static std::map<std::vector<int>, int*> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if (auto f = cache.find(key); f != cache.end()) return f->second;
+  const int per = nseq * p.nq;
+  std::vector<std::pair<long, int>> cost(nitems);
+  for (int w0 = 0; w0 < nitems; ++w0) {
+    const int sp = w0 % p.nsplit, w = w0 / p.nsplit;
+    const int qt = p.ntq - 1 - w / per, seq = (w % per) / p.nq;
+    const int P = p.P[seq], ps = p.pos_start[seq];
+    long c = 0;
+    if (qt * BM < P) {
+      const int qf = ps + qt * BM, ql = std::min(ps + P, qf + BM) - 1;
+      const int lo = p.window > 0 ? std::max(0, qf - p.window + 1) : 0;
+      int x0 = lo / BN, x1 = ql / BN + 1;
+      if (p.nsplit > 1) {
+        int a, b;
+        split_range(x0, x1, p.nsplit, sp, a, b);
+        x0 = a;
+        x1 = std::max(a, b);
+      }
+      if (x1 > x0) c = x1 - x0 + 2;
+    }
+    cost[w0] = {c, w0};
   }
   std::stable_sort(cost.begin(), cost.end(),
                    [](const auto& a, const auto& b) { return a.first > b.first; });
