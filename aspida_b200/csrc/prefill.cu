@@ -1187,11 +1187,6 @@ bool make_map(CUtensorMap* m, const void* base, long cols, long rows, int box_ro
 // deals items boustrophedon-wise).
 const int* two_tile_schedule(const PrefillParams& p, int nseq, int nitems, int grid,
                              cudaStream_t st) {
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return nullptr;                       // no synchronous upload inside a capture
-  }
   constexpr int BN = 128;
   std::vector<int> key = {grid, nitems, nseq, p.nq, p.ntq, p.window};
   for (int s = 0; s < nseq; ++s) { key.push_back(p.P[s]); key.push_back(p.pos_start[s]); }
@@ -1202,6 +1197,11 @@ const int* two_tile_schedule(const PrefillParams& p, int nseq, int nitems, int g
   static std::map<std::vector<int>, int*> cache;
   std::lock_guard<std::mutex> lk(mu);
   if (auto f = cache.find(key); f != cache.end()) return f->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;                       // no synchronous upload inside a capture
+  }
   const int per = nseq * p.nq;
   std::vector<std::pair<long, int>> cost(nitems);
   for (int w = 0; w < nitems; ++w) {
@@ -1250,11 +1250,6 @@ const int* two_tile_schedule(const PrefillParams& p, int nseq, int nitems, int g
 // split) costs its key tiles (64 keys) plus 2.
 const int* one_tile_schedule(const PrefillParams& p, int nseq, int nitems, int grid,
                              cudaStream_t st) {
-  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-    cudaGetLastError();
-    return nullptr;
-  }
   constexpr int BN = 64;
   std::vector<int> key = {-1, grid, nitems, nseq, p.nq, p.ntq, p.window, p.nsplit};
   for (int s = 0; s < nseq; ++s) { key.push_back(p.P[s]); key.push_back(p.pos_start[s]); }
@@ -1265,6 +1260,11 @@ const int* one_tile_schedule(const PrefillParams& p, int nseq, int nitems, int g
   static std::map<std::vector<int>, int*> cache;
   std::lock_guard<std::mutex> lk(mu);
   if (auto f = cache.find(key); f != cache.end()) return f->second;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return nullptr;                       // no synchronous upload inside a capture
+  }
   const int per = nseq * p.nq;
   std::vector<std::pair<long, int>> cost(nitems);
   for (int w0 = 0; w0 < nitems; ++w0) {
