@@ -48,7 +48,8 @@ def oracle_decode(oracle, q, Ks, Vs, pos, nq, nkv, hd, **kw):
 
 
 @pytest.mark.parametrize("hd,nq,nkv", [(64, 32, 8), (128, 32, 8), (128, 64, 8), (256, 16, 8),
-                                       (128, 8, 8), (64, 8, 1), (128, 12, 4)])
+                                       (128, 8, 8), (64, 8, 1), (128, 12, 4), (256, 8, 2),
+                                       (256, 3, 1)])
 def test_decode_shapes(ab, oracle, hd, nq, nkv):
     lens = [1, 15, 16, 17, 100, 333, 1000, 2049]
     q, Ks, Vs = make_batch(lens, nq, nkv, hd, seed=hd + nq)
@@ -117,10 +118,11 @@ def test_decode_is_deterministic(ab):
     assert np.array_equal(a, b)
 
 
-def test_partial_and_merge(ab, oracle):
+@pytest.mark.parametrize("hd,nq", [(128, 64), (256, 16)])
+def test_partial_and_merge(ab, oracle, hd, nq):
     """Sequence-parallel decode: split the keys of one long sequence into S
     slices, compute partials, merge; equals whole-range decode."""
-    L, nq, nkv, hd = 20000, 64, 8, 128
+    L, nkv = 20000, 8
     q, Ks, Vs = make_batch([L], nq, nkv, hd, seed=5)
     K, V = Ks[0], Vs[0]
     cuts = [0, 5000, 5001, 12000, 12000, L]     # includes an empty slice
