@@ -26,6 +26,7 @@ SIGNATURES = {
     "aspida_gpu_last_error": (i32, []),
     "aspida_gpu_fattn_kv": (i32, [i32, pp, pp, ip, ip]),
     "aspida_attn_device_status": (i32, []),
+    "aspida_attn_device_status_where": (i32, []),
     "aspida_attn_debug_fail_allocs": (None, [i32]),
     "aspida_attn_prep": (i32, [vp, vp, vp, i32, i32, i32, i32, vp, vp, f32, vp, i32, vp, vp,
                                i32, i32, i32, f32, f32, f32, i32, f32, f32, vp, i32, i32, i32,
@@ -56,6 +57,8 @@ SIGNATURES = {
     "aspida_attn_peer_close": (i32, [vp]),
     "aspida_attn_peer_free": (i32, [vp]),
     "aspida_attn_exchange_merge": (i32, [vp, vp, i32, i32, C.c_ulonglong, vp, vp, i32, i32, vp]),
+    "aspida_attn_exchange_merge_ex": (i32, [vp, vp, i32, i32, C.c_ulonglong, vp, vp, i32, i32,
+                                            vp, C.c_longlong, vp]),
     "aspida_attn_merge": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, vp]),
     "aspida_attn_merge_strided": (i32, [vp, vp, vp, vp, vp, i32, i32, i32, C.c_long, vp]),
     "aspida_attn_decode_noalloc": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32, i32,

@@ -21,7 +21,7 @@ int num_sms();                                 // SM count of the current device
 // Device-side status word: a kernel whose bounded wait ran out writes a
 // non-zero code here and returns early; aspida_attn_device_status() reads it.
 struct DeviceStatus { int code; int where; };
-DeviceStatus* device_status_ptr();             // per-device, lazily allocated
+DeviceStatus* device_status_ptr();             // per-device compiled-in word (no allocation)
 
 constexpr int kDevTimeoutMbar = 1;             // mbarrier wait ran out
 

@@ -73,18 +73,23 @@ int num_sms() {
   return cached[dev];
 }
 
+// The status word is a file-scope device variable: every device that loads
+// the library holds its own zero-initialised copy, so looking it up needs no
+// allocation and no synchronisation (safe on a capturing stream). Host code
+// only knows a stand-in for the symbol; the device address is resolved per
+// device, with that device current, and cached.
+static __device__ __align__(16) DeviceStatus g_dev_status;
+
 DeviceStatus* device_status_ptr() {
   static std::mutex mu;
   static DeviceStatus* per_dev[64] = {nullptr};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  if (dev < 0 || dev >= 64) return nullptr;
   std::lock_guard<std::mutex> lk(mu);
   if (!per_dev[dev]) {
     void* p = nullptr;
-    if (cudaMalloc(&p, sizeof(DeviceStatus)) != cudaSuccess) return nullptr;
-    cudaMemset(p, 0, sizeof(DeviceStatus));
-    cudaDeviceSynchronize();
+    if (cudaGetSymbolAddress(&p, g_dev_status) != cudaSuccess) return nullptr;
     per_dev[dev] = static_cast<DeviceStatus*>(p);
   }
   return per_dev[dev];
@@ -250,17 +255,27 @@ extern "C" int aspida_gpu_fattn_kv(int handle, void** K, void** V, int* max_len,
 
 extern "C" int aspida_attn_device_status(void) {
   DeviceStatus* d = device_status_ptr();
-  if (!d) return record_status(ASPIDA_ERR_NOMEM);
+  if (!d) return record_status(ASPIDA_ERR_UNSUPPORTED);
   cudaError_t e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return record_status((int)e);
   DeviceStatus h{0, 0};
-  cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  e = cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return record_status((int)e);
   if (h.code != 0) {
-    cudaMemset(d, 0, sizeof(DeviceStatus));
-    cudaDeviceSynchronize();
+    const DeviceStatus zero{0, 0};
+    cudaMemcpy(d, &zero, sizeof(zero), cudaMemcpyHostToDevice);
     return record_status(ASPIDA_ERR_DEVICE);
   }
   return 0;
+}
+
+extern "C" int aspida_attn_device_status_where(void) {
+  DeviceStatus* d = device_status_ptr();
+  if (!d) return record_status(ASPIDA_ERR_UNSUPPORTED);
+  DeviceStatus h{0, 0};
+  cudaError_t e = cudaMemcpy(&h, d, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return record_status((int)e);
+  return h.code ? h.where : 0;
 }
 
 extern "C" void aspida_attn_debug_fail_allocs(int n) { g_fail_allocs.store(n > 0 ? n : 0); }

@@ -40,13 +40,13 @@ namespace {
 constexpr size_t kNoAllocBytes = 16u << 20;   // 16 MiB of decode scratch per GPU
 
 static __device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocBytes];
-static __device__ __align__(256) aspida::DeviceStatus g_noalloc_status;
 
 struct Addrs { void* ws = nullptr; aspida::DeviceStatus* status = nullptr; };
 std::mutex g_mu;
 Addrs g_addrs[64];
 
-// Device addresses of the arrays on the current device (looked up once).
+// Device addresses of the scratch array and the status word on the current
+// device (looked up once).
 int lookup(Addrs& out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -56,13 +56,12 @@ int lookup(Addrs& out) {
   Addrs& a = g_addrs[dev];
   if (!a.ws) {
     void* ws = nullptr;
-    void* st = nullptr;
     e = cudaGetSymbolAddress(&ws, g_noalloc_ws);
     if (e != cudaSuccess) return aspida::record_status((int)e);
-    e = cudaGetSymbolAddress(&st, g_noalloc_status);
-    if (e != cudaSuccess) return aspida::record_status((int)e);
+    aspida::DeviceStatus* st = aspida::device_status_ptr();   // compiled in, no allocation
+    if (!st) return aspida::record_status(ASPIDA_ERR_UNSUPPORTED);
     a.ws = ws;
-    a.status = static_cast<aspida::DeviceStatus*>(st);
+    a.status = st;
   }
   out = a;
   return 0;

@@ -31,6 +31,7 @@ namespace aspida {
 namespace {
 
 constexpr int kMaxWorld = 8;
+constexpr long long kDefaultWaitLimit = 1LL << 22;   // flag polls: seconds with the backoff
 
 struct PeerArgs {
   float* recv[kMaxWorld];       // every rank's receive buffer (this rank's mapping)
@@ -38,6 +39,8 @@ struct PeerArgs {
   const float* gate;
   float* out;
   DeviceStatus* status;
+  int* fail_word;               // optional caller word (e.g. host-mapped), set on timeout
+  long long wait_limit;         // polls per flag before giving up
   long per;                     // floats per partial: rows * (hd + 2)
   long stride;                  // floats per slot: per rounded up to 4 (16-byte slots)
   long bank_floats;             // floats of one bank's slots
@@ -86,9 +89,13 @@ __global__ void __launch_bounds__(256) exchange_merge_kernel(const PeerArgs a) {
       uint32_t ns = 32;
       long it = 0;
       while (ld_acquire_sys(myfl + s) != a.tag) {
-        if (++it > (1L << 22)) {                    // ~seconds with the backoff below
+        if (++it > a.wait_limit) {                  // default limit: ~seconds with the backoff
           ok = 0;
           if (a.status) { atomicExch(&a.status->code, kDevTimeoutMbar); a.status->where = 60; }
+          if (a.fail_word) {
+            *(volatile int*)a.fail_word = kDevTimeoutMbar;
+            __threadfence_system();
+          }
           break;
         }
         if (it > 1024) {
@@ -194,12 +201,14 @@ extern "C" int aspida_attn_peer_free(void* ptr) {
   return cuda_status(cudaFree(ptr));
 }
 
-extern "C" int aspida_attn_exchange_merge(const float* part, void* const* recv, int world,
-                                          int rank, unsigned long long step, const float* gate,
-                                          float* out, int rows, int hd, void* stream) {
+extern "C" int aspida_attn_exchange_merge_ex(const float* part, void* const* recv, int world,
+                                             int rank, unsigned long long step,
+                                             const float* gate, float* out, int rows, int hd,
+                                             int* fail_word, long long wait_limit,
+                                             void* stream) {
   if (rows <= 0) return 0;
   if (!part || !recv || !out || world <= 0 || world > kMaxWorld || rank < 0 || rank >= world ||
-      hd <= 0 || step == 0 || ((uintptr_t)part & 15))
+      hd <= 0 || step == 0 || ((uintptr_t)part & 15) || wait_limit < 0)
     return record_status(ASPIDA_ERR_ARG);
   PeerArgs a{};
   for (int s = 0; s < world; ++s) {
@@ -211,6 +220,8 @@ extern "C" int aspida_attn_exchange_merge(const float* part, void* const* recv, 
   a.gate = gate;
   a.out = out;
   a.status = device_status_ptr();
+  a.fail_word = fail_word;
+  a.wait_limit = wait_limit > 0 ? wait_limit : kDefaultWaitLimit;
   a.world = world;
   a.rank = rank;
   a.rows = rows;
@@ -222,4 +233,11 @@ extern "C" int aspida_attn_exchange_merge(const float* part, void* const* recv, 
   exchange_merge_kernel<<<blocks, 256, 0, (cudaStream_t)stream>>>(a);
   ASPIDA_CHECK_LAUNCH();
   return 0;
+}
+
+extern "C" int aspida_attn_exchange_merge(const float* part, void* const* recv, int world,
+                                          int rank, unsigned long long step, const float* gate,
+                                          float* out, int rows, int hd, void* stream) {
+  return aspida_attn_exchange_merge_ex(part, recv, world, rank, step, gate, out, rows, hd,
+                                       nullptr, 0, stream);
 }

@@ -103,7 +103,7 @@ class PeerExchange:
     rank's buffer. ``__call__`` runs one step: all ranks must call it once per
     step, in the same order (the step number tags the arrivals)."""
 
-    def __init__(self, rows: int, hd: int, group=None):
+    def __init__(self, rows: int, hd: int, group=None, wait_limit: int = 0):
         import ctypes as C
         import torch.distributed as dist
         from . import _lib
@@ -114,6 +114,13 @@ class PeerExchange:
         if self.world > 8:
             raise ValueError("the peer exchange supports up to 8 ranks")
         self.rows, self.hd, self.step = rows, hd, 0
+        # The kernel sets this pinned (device-visible) word when its wait for a
+        # peer runs out; the host reads it without synchronising the stream.
+        # After a timeout the two-bank reuse guarantee no longer holds, so the
+        # exchange refuses every further step.
+        self.wait_limit = int(wait_limit)
+        self.fail_word = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.failed = False
         # every rank takes part in the same collectives whatever fails
         # locally, so a failure is seen by all ranks and none is left waiting
         nbytes = self._lib.aspida_attn_peer_buffer_size(self.world, rows, hd)
@@ -154,14 +161,28 @@ class PeerExchange:
     def __call__(self, part: torch.Tensor, out: torch.Tensor, gate: Optional[torch.Tensor] = None,
                  stream=None) -> torch.Tensor:
         from .attention import GPUError, _stream
+        self._raise_if_failed()
         self.step += 1
-        rc = self._lib.aspida_attn_exchange_merge(
+        rc = self._lib.aspida_attn_exchange_merge_ex(
             part.data_ptr(), self.table, self.world, self.rank, self.step,
             None if gate is None else gate.data_ptr(), out.data_ptr(), self.rows, self.hd,
-            _stream(stream))
+            self.fail_word.data_ptr(), self.wait_limit, _stream(stream))
         if rc:
             raise GPUError(rc, "exchange_merge")
         return out
+
+    def _raise_if_failed(self):
+        if self.failed or int(self.fail_word[0]) != 0:
+            self.failed = True
+            raise ShardError(f"peer exchange timed out waiting for a rank (step {self.step}); "
+                             "its buffers are no longer usable")
+
+    def check(self, stream=None):
+        """Wait for the last step on ``stream`` and raise :class:`ShardError`
+        if any exchange so far gave up waiting for a peer. Without this call
+        a timeout is raised at the start of the next step."""
+        (stream or torch.cuda.current_stream()).synchronize()
+        self._raise_if_failed()
 
     def close(self, barrier: bool = True):
         """Unmap the peers' buffers and free this rank's (after a barrier, so
@@ -227,6 +248,12 @@ class SeqParallelDecode:
         if self.px is not None:
             self.px.close()
             self.px = None
+
+    def check(self, stream=None):
+        """Raise :class:`ShardError` if an exchange so far timed out (p2p
+        transport; waits for the stream first)."""
+        if self.px is not None:
+            self.px.check(stream)
 
     def __call__(self, q: torch.Tensor, gate: Optional[torch.Tensor] = None,
                  stream=None) -> torch.Tensor:

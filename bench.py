@@ -82,18 +82,36 @@ def peaks_tensor():
     return 1590.0, "fallback"
 
 
-def traffic_from_profile():
-    """dram bytes per decode call from the committed ncu summary, if any."""
-    p = os.path.join(ROOT, "profiles", "decode_cfg2.md")
-    if not os.path.exists(p):
+def traffic(leg):
+    """DRAM bytes per launch of a leg's dominant kernel, from the ncu capture
+    figures recorded in profiles/ncu_traffic.json (None if absent)."""
+    p = os.path.join(ROOT, "profiles", "ncu_traffic.json")
+    try:
+        with open(p) as f:
+            return int(json.load(f)[leg]["traffic_bytes"])
+    except (OSError, KeyError, ValueError, TypeError):
         return None
-    for line in open(p):
-        if line.startswith("traffic_bytes_per_call:"):
-            try:
-                return int(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+
+
+def cpu_model():
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
+def config(world, kv_bytes_per_gpu):
+    """The workload description, identical in both arms."""
+    return {"workload": "cfg2 batched GQA decode: B=32 per GPU, 32/8 heads, hd128, fp16 KV, "
+                        "len~U[512,8192]",
+            "global_batch": B * world, "kv_bytes_per_gpu": int(kv_bytes_per_gpu),
+            "parallelism": f"dp{world} (sequence sharding, no collective)",
+            "l2": "inputs (~570 MB KV per GPU) larger than the 126 MB L2; no flush"}
 
 
 class ClockSampler:
@@ -161,7 +179,7 @@ def cpu_baseline(lens_list, seconds, K_host, V_host, q_host):
             break
     per = el / reps
     return {"value": algo_bytes(lens_list) / per / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "port",
+            "cpu_model": cpu_model(), "kind": "port",
             "sample": f"full cfg-2 batch (B=32, {sum(lens_list)} keys), {reps} reps in {el:.1f} s, "
                       "C++ restatement of the Ada attention loops, one (seq x head) job per task"}
 
@@ -383,7 +401,7 @@ def prefill_cpu_sample(q, K, V, seconds=8.0):
             break
     fl = sum(nq * 4 * hd * (r + 1) for r in rows)
     return {"value": round(fl * reps / el / 1e12, 5), "unit": "TFLOP/s", "cores": threads,
-            "kind": "port", "sample": f"last 16 query rows of one 4096-token sequence, {reps} reps"}
+            "cpu_model": cpu_model(), "kind": "port", "sample": f"last 16 query rows of one 4096-token sequence, {reps} reps"}
 
 
 def host_batch(seed, lens):
@@ -426,10 +444,11 @@ def run_reference(args, rank):
         "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
         "ms_per_step": round(per * 1e3, 3), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "cfg2 batched GQA decode (B=32, 32/8, hd128, len~U[512,8192])",
-                   "global_batch": B, "parallelism": "rank 0 only (host CPU)"},
-        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"full cfg-2 batch, {len(times)} timed steps"},
+        "config": config(max(1, int(os.environ.get("WORLD_SIZE", args.gpus))), algo_bytes(lens)),
+        "cpu_baseline": {"value": round(val, 3), "unit": "GB/s", "cores": threads,
+                         "cpu_model": cpu_model(), "kind": "port",
+                         "sample": f"full cfg-2 batch (rank 0's, host CPU), {len(times)} timed "
+                                   "steps"},
         "e2e": {"value": round(val, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -591,7 +610,6 @@ def main():
     if rank == 0:
         hbm, src = peaks()
         achieved = nbytes / (ms * 1e-3) / 1e9
-        traffic = traffic_from_profile()
         line = {
             "metric": METRIC,
             "value": round(bytes_all / (ms_max * 1e-3) / 1e9, 3),
@@ -605,14 +623,10 @@ def main():
             "vs_baseline": None,
             "dtype": "f16 KV / f32 accumulate",
             "data": "synthetic (seeded N(0,1) fp16 KV, lengths U[512,8192])",
-            "config": {"workload": "cfg2 batched GQA decode: B=32 per GPU, 32/8 heads, hd128, "
-                                   "fp16 KV, len~U[512,8192]",
-                       "global_batch": B * world, "kv_bytes_per_gpu": nbytes,
-                       "parallelism": f"dp{world} (sequence sharding, no collective)",
-                       "l2": "inputs (~570 MB KV per GPU) larger than the 126 MB L2; no flush"},
+            "config": config(world, nbytes),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm,
                          "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                         "traffic": traffic, "peak_source": f"{src} hbm_gbs (copy, burst)"},
+                         "traffic": traffic("decode_cfg2"), "peak_source": f"{src} hbm_gbs (copy, burst)"},
             "e2e": {"value": round(bytes_all / (ms_e2e_max * 1e-3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": int(qp.numel() * 4 + kp.numel() * 4 + vp.numel() * 4
                                               + B * (2 * 4 + 2 * 8)),
@@ -629,7 +643,7 @@ def main():
                              "achieved": round(p_flops / (p_ms * 1e-3) / 1e12, 2),
                              "peak": peaks_tensor()[0], "unit": "TFLOP/s",
                              "frac": round(p_flops / (p_ms * 1e-3) / 1e12 / peaks_tensor()[0], 4),
-                             "traffic": None,
+                             "traffic": traffic("prefill_cfg3"),
                              "peak_source": f"{peaks_tensor()[1]} bf16_tflops (cuBLAS, burst)"},
                 "gpu_launches": p_steps,
             },
@@ -653,7 +667,8 @@ def main():
             "bytes_per_step_per_gpu": int(q_bytes),
             "roofline": {"bound": "hbm", "achieved": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
                          "peak": peaks()[0], "unit": "GB/s",
-                         "frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks()[0], 4)},
+                         "frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks()[0], 4),
+                         "traffic": traffic("decode_q8_cfg2")},
             "gpu_launches": args.steps * 2,
         }
         hbm_peak, tc_peak = peaks()[0], peaks_tensor()[0]

@@ -77,8 +77,17 @@ int aspida_gpu_fattn_kv(int handle, void** K, void** V, int* max_len, int* kvd);
 
 /* Synchronise the current device and return (then clear) the device status
  * word that a kernel sets when one of its bounded waits runs out:
- * 0 = none, ASPIDA_ERR_DEVICE otherwise. */
+ * 0 = none, ASPIDA_ERR_DEVICE otherwise. The word is compiled into the
+ * library (one per device), so no call allocates or synchronises to set it
+ * up; every entry point, aspida_attn_decode_noalloc included, reports there. */
 int aspida_attn_device_status(void);
+
+/* Where the device status word was set (a code identifying the wait that
+ * ran out: 10/11 decode producer/consumer, 60 the peer exchange's flag
+ * wait; other values name mbarrier waits of the prefill kernel), or 0 if
+ * it is clear. Does not synchronise or clear; call it before
+ * aspida_attn_device_status(), after the work has finished. */
+int aspida_attn_device_status_where(void);
 
 /* Test hook: make the next `n` device allocations made by the library fail
  * (as cudaMalloc would on an exhausted device). n = 0 disarms it. */
@@ -284,6 +293,23 @@ int aspida_attn_exchange_merge(const float* part, void* const* recv, int world, 
                                unsigned long long step, const float* gate, float* out, int rows,
                                int hd, void* stream);
 
+/* aspida_attn_exchange_merge with two more arguments (no counterpart in the
+ * reference):
+ *   fail_word   int the kernel sets to a non-zero code when its wait runs
+ *               out, besides the device status word; NULL = none. Pinned
+ *               host memory (device-visible) lets the host see a failed
+ *               exchange without synchronising the stream.
+ *   wait_limit  flag polls per rank before the wait gives up (0 = the
+ *               default of ~4M polls with backoff, seconds); a short limit
+ *               lets a test make the wait run out quickly.
+ * When the wait runs out the kernel writes no output and returns; the
+ * exchange's two-bank reuse guarantee is then void, so the caller must not
+ * run further steps on these buffers. */
+int aspida_attn_exchange_merge_ex(const float* part, void* const* recv, int world, int rank,
+                                  unsigned long long step, const float* gate, float* out,
+                                  int rows, int hd, int* fail_word, long long wait_limit,
+                                  void* stream);
+
 /* ------------------------------------------------------------------------
  * Causal prefill attention on the tcgen05 tensor cores.
  * Replaces aspida_ggml_fattn_prefill (gpu/fattn_ggml.cuh:109-141) and the
@@ -355,7 +381,9 @@ int aspida_attn_step_host(const int* handles, int B, const float* q, const float
  * aspida_attn_decode_workspace_size of the call exceeds that (e.g. B > ~360
  * at nkv 8, hd 128). The first call on each device looks up the array's
  * device address; make it before any stream capture. All calls share the
- * array, so calls that overlap on the GPU race: serialise them. */
+ * array, so calls that overlap on the GPU race: serialise them. A bounded
+ * wait that runs out is reported by aspida_attn_device_status(), as for the
+ * other entry points. */
 int aspida_attn_decode_noalloc(const float* q, const float* gate, const void* const* K,
                                const void* const* V, const int* pos, const int* max_len,
                                float* out, int B, int nq, int nkv, int hd, float scale,

@@ -1,4 +1,5 @@
-"""Sequence-parallel decode on 2 GPUs (skipped with fewer): each rank attends
+"""Sequence-parallel decode on 2 GPUs (skipped with fewer), at config 5a's
+length (one 131072-key sequence, 64/8 heads, hd 128): each rank attends
 its KV chunk of one long sequence, the (m, l, o) partials are exchanged
 (NVLink peer stores fused with the merge, or an NCCL all-gather) and merged;
 every rank's output must match the CPU oracle, on every one of several
@@ -33,7 +34,7 @@ def _worker(rank, world, port, ret, transport):
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
                             timeout=datetime.timedelta(seconds=60))
     from aspida_b200 import shard
-    nq, nkv, hd, L = 64, 8, 128, 20000
+    nq, nkv, hd, L = 64, 8, 128, 131072
     g = torch.Generator().manual_seed(7)
     K = torch.randn(L, nkv * hd, generator=g).half()
     V = torch.randn(L, nkv * hd, generator=g).half()
@@ -61,7 +62,7 @@ def test_seq_parallel_decode(oracle, transport):
     ret = mp.Manager().dict()
     mp.start_processes(_worker, args=(world, _free_port(), ret, transport), nprocs=world,
                        join=True, start_method="spawn")
-    nq, nkv, hd, L = 64, 8, 128, 20000
+    nq, nkv, hd, L = 64, 8, 128, 131072
     g = torch.Generator().manual_seed(7)
     K = torch.randn(L, nkv * hd, generator=g).half().float().numpy()
     V = torch.randn(L, nkv * hd, generator=g).half().float().numpy()
