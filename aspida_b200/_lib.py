@@ -49,6 +49,9 @@ SIGNATURES = {
     "aspida_attn_decode_q8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
                                     i32, f32, i32, i32, vp, sz, vp]),
     "aspida_attn_quantize_q8": (i32, [vp, vp, vp, C.c_longlong, vp]),
+    "aspida_attn_decode_fp8": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, f32,
+                                     i32, f32, i32, i32, vp, sz, vp]),
+    "aspida_attn_quantize_fp8": (i32, [vp, vp, vp, C.c_longlong, vp]),
     "aspida_attn_prefill_q8_gated": (i32, [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32,
                                            vp]),
     "aspida_attn_peer_buffer_size": (sz, [i32, i32, i32]),

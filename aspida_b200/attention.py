@@ -311,6 +311,51 @@ def decode_q8(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor, Ks_tab:
     return out
 
 
+def quantize_fp8(x: torch.Tensor, q: Optional[torch.Tensor] = None,
+                 scales: Optional[torch.Tensor] = None, stream=None):
+    """fp8 (e4m3) quantisation of f32 x [..., n] (n a multiple of 32) into
+    uint8 codes q [..., n] and fp16 scales [..., n/32] (per 32-value block,
+    s = fp16(max|v| / 448), code = e4m3(v / s), saturating)."""
+    if x.dtype != torch.float32 or not x.is_contiguous() or x.shape[-1] % 32:
+        raise ValueError("x must be contiguous f32 with a last dim divisible by 32")
+    if q is None:
+        q = torch.empty(x.shape, dtype=torch.uint8, device=x.device)
+    if scales is None:
+        scales = torch.empty((*x.shape[:-1], x.shape[-1] // 32), dtype=torch.float16,
+                             device=x.device)
+    if q.numel() != x.numel() or scales.numel() * 32 != x.numel() or not q.is_contiguous() \
+            or not scales.is_contiguous():
+        raise ValueError("q / scales do not match x")
+    rc = _lib_().aspida_attn_quantize_fp8(_ptr(x), _ptr(q), _ptr(scales), x.numel() // 32,
+                                          _stream(stream))
+    _check(rc, "quantize_fp8")
+    return q, scales
+
+
+def decode_fp8(q: torch.Tensor, K_tab: torch.Tensor, V_tab: torch.Tensor, Ks_tab: torch.Tensor,
+               Vs_tab: torch.Tensor, pos: torch.Tensor, nq: int, nkv: int, hd: int, *,
+               gate: Optional[torch.Tensor] = None, max_len: Optional[torch.Tensor] = None,
+               scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
+               max_kv_len: int, chunk: int = 0, out: Optional[torch.Tensor] = None,
+               workspace: Optional[Workspace] = None, stream=None) -> torch.Tensor:
+    """Batched GQA decode over fp8 (e4m3) caches: K_tab/V_tab pointer tables of
+    uint8 code caches [rows, nkv*hd], Ks_tab/Vs_tab of fp16 block scales
+    [rows, nkv*hd/32] (quantize_fp8's layout)."""
+    B = q.shape[0]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((B, nq * hd), dtype=torch.float32, device=q.device)
+    nbytes = decode_workspace_size(B, nq, nkv, hd, max_kv_len, chunk)
+    wsb = _ws(workspace, q.device).get(nbytes, q.device)
+    rc = _lib_().aspida_attn_decode_fp8(
+        _ptr(q), _ptr(gate), _ptr(K_tab), _ptr(V_tab), _ptr(Ks_tab), _ptr(Vs_tab), _ptr(pos),
+        _ptr(max_len), _ptr(out), B, nq, nkv, hd, scale, window, softcap, max_kv_len, chunk,
+        _ptr(wsb), wsb.numel(), _stream(stream))
+    _check(rc, "decode_fp8")
+    return out
+
+
 def prefill_q8_gated(q: torch.Tensor, K8: torch.Tensor, V8: torch.Tensor, Ks: torch.Tensor,
                      Vs: torch.Tensor, nq: int, nkv: int, hd: int, pos_start: int = 0, *,
                      gate: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,

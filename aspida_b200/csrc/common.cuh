@@ -143,6 +143,54 @@ __device__ __forceinline__ float rope_angle(int i, int pos_eff, int rd, float ba
   return th;
 }
 
+// RoPE parameters of the pre-attention step (LLM_RoPE.Apply_Sections,
+// src/llm/llm_rope.adb:84-200; k_fattn_prep, gpu/gpu_matvec.cu:1449-1503).
+struct RopeArgs {
+  const float* ff;          // per-pair frequency divisors, or null
+  float base, freq_scale, m_scale, corr_lo, corr_hi;
+  int rd, yarn_on, use_ff, interleaved, sec_total;
+};
+
+// One warp normalises one head row: sh[d] <- x[d] / rms * w[d] (or x[d]
+// without weights), rms = sqrt(sum x^2 / hd + eps). The sum is reduced in a
+// fixed order (lane-strided partial sums, then a butterfly), so every user
+// of this helper - the prep kernel and the fused decode's appends - writes
+// bit-identical rows. sh: hd floats of shared memory owned by the warp.
+__device__ __forceinline__ void warp_norm_row(const float* __restrict__ x,
+                                              const float* __restrict__ w, float eps, int hd,
+                                              float* sh, int lane) {
+  float ss = 0.f;
+  for (int d = lane; d < hd; d += 32) {
+    const float v = x[d];
+    sh[d] = v;
+    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  }
+  if (w) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss = __fadd_rn(ss, __shfl_xor_sync(0xffffffffu, ss, o));
+    const float rms = sqrtf(ss / (float)hd + eps);
+    for (int d = lane; d < hd; d += 32) sh[d] = __fmul_rn(sh[d] / rms, w[d]);
+  }
+  __syncwarp();
+}
+
+// Rotation of pair i (0 <= i < rd/2) of a normalised row: the pair's two
+// dims d1 < d2 (NeoX: i, i + rd/2; interleaved: 2i, 2i + 1) and their
+// rotated values. Pairs i >= sec_total rotate at position 0 (the reference's
+// section quirk). One angle per pair.
+__device__ __forceinline__ void rope_pair(const float* sh, int i, int pos, const RopeArgs& r,
+                                          int& d1, int& d2, float& o1, float& o2) {
+  if (r.interleaved) { d1 = 2 * i; d2 = d1 + 1; }
+  else { d1 = i; d2 = i + r.rd / 2; }
+  const int pos_eff = i < r.sec_total ? pos : 0;
+  const float th = rope_angle(i, pos_eff, r.rd, r.base, r.freq_scale, r.yarn_on, r.corr_lo,
+                              r.corr_hi, r.ff, r.use_ff);
+  const float c = __fmul_rn(cosf(th), r.m_scale), sn = __fmul_rn(sinf(th), r.m_scale);
+  const float x1 = sh[d1], x2 = sh[d2];
+  o1 = __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn));
+  o2 = __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
+}
+
 __device__ __forceinline__ uint32_t lds_u32(uint32_t saddr) {
   uint32_t v;
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(saddr));

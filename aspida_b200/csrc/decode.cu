@@ -37,6 +37,8 @@
 #include <type_traits>
 #include <cmath>
 
+#include <cuda_fp8.h>
+
 #include "common.cuh"
 
 namespace aspida {
@@ -62,6 +64,7 @@ struct DecodeParams {
   const int8_t* const* V8;
   const __half* const* Ks;    // ... and fp16 scales [rows][nkv*hd/32]
   const __half* const* Vs;
+  int f8;                     // the 8-bit caches hold fp8 e4m3 values, not int8
   const __half* Kpool;  // paged form: shared pools of blocks of block_size rows
   const __half* Vpool;
   const int* block_table;   // [B][max_blocks] block ids, or null (per-sequence caches)
@@ -206,6 +209,26 @@ __device__ __forceinline__ uint32_t i8pair_to_h2(uint32_t biased, uint32_t sel) 
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// Two 8-bit cache values -> fp16x2, exactly: bytes (0, 1) of w for sel
+// 0x4140, bytes (2, 3) for 0x4342. int8 (F8 = false): w pre-xored with
+// 0x80808080, i8pair_to_h2. fp8 e4m3 (F8 = true): every e4m3 value is an
+// fp16 value, one cvt per pair.
+template <bool F8>
+__device__ __forceinline__ uint32_t kv8_to_h2(uint32_t w, uint32_t sel) {
+  if constexpr (F8) {
+    const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)(sel == 0x4140u ? (w & 0xffffu) : (w >> 16));
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+    return (uint32_t)h.x | ((uint32_t)h.y << 16);
+  } else {
+    return i8pair_to_h2(w, sel);
+  }
+}
+// The bias that the int8 conversion expects; fp8 words are used as stored.
+template <bool F8>
+__device__ __forceinline__ uint32_t kv8_bias(uint32_t w) {
+  return F8 ? w : (w ^ 0x80808080u);
+}
+
 // Byte offset of stage row k (0..15) within one side of a stage.
 template <class Geo>
 __device__ __forceinline__ int row_off(int k) {
@@ -324,10 +347,9 @@ __device__ __forceinline__ void fuse_q(const DecodeParams& p, float (&qv)[HD / 1
 }
 
 // One warp appends sequence b's new row for kv head kvh at position pos:
-// V as given, K RMSNorm'ed (optional) and rotated, both to fp16 - the
-// arithmetic of prep_kernel, in the same order (sequential sum of squares,
-// the same angle function), so the cache rows are identical. sh: HD floats
-// of scratch for the warp.
+// V as given, K RMSNorm'ed (optional) and rotated, both to fp16 - through the
+// same warp helpers as prep_kernel (warp_norm_row, rope_pair), so the cache
+// rows are identical. sh: HD floats of scratch for the warp.
 template <int HD>
 __device__ void append_row(const DecodeParams& p, int b, int kvh, int pos, float* sh, int lane) {
   const long kvd = (long)p.nkv * HD;
@@ -335,61 +357,20 @@ __device__ void append_row(const DecodeParams& p, int b, int kvh, int pos, float
   const float* vr = p.v_new + (long)b * kvd + (long)kvh * HD;
   __half* Kc = const_cast<__half*>(p.K[b]) + (long)pos * kvd + (long)kvh * HD;
   __half* Vc = const_cast<__half*>(p.V[b]) + (long)pos * kvd + (long)kvh * HD;
-  for (int d = lane; d < HD; d += 32) {
-    Vc[d] = __float2half_rn(vr[d]);
-    sh[d] = kr[d];
+  for (int d = lane; d < HD; d += 32) Vc[d] = __float2half_rn(vr[d]);
+  warp_norm_row(kr, p.k_norm, p.eps, HD, sh, lane);
+  RopeArgs r;
+  r.ff = p.ff; r.base = p.rbase; r.freq_scale = p.freq_scale; r.m_scale = p.m_scale;
+  r.corr_lo = p.corr_lo; r.corr_hi = p.corr_hi; r.rd = p.rd; r.yarn_on = p.yarn_on;
+  r.use_ff = p.use_ff; r.interleaved = p.interleaved; r.sec_total = p.sec_total;
+  for (int i = lane; i < p.rd / 2; i += 32) {
+    int d1, d2;
+    float o1, o2;
+    rope_pair(sh, i, pos, r, d1, d2, o1, o2);
+    Kc[d1] = __float2half_rn(o1);
+    Kc[d2] = __float2half_rn(o2);
   }
-  __syncwarp();
-  float rms = 1.f;
-  if (p.k_norm) {
-    float ss = 0.f;
-    if (lane == 0)
-      for (int i = 0; i < HD; ++i) ss = __fadd_rn(ss, __fmul_rn(sh[i], sh[i]));
-    ss = __shfl_sync(0xffffffffu, ss, 0);
-    rms = sqrtf(ss / (float)HD + p.eps);
-  }
-  float nv[HD / 32];
-#pragma unroll
-  for (int j = 0; j < HD / 32; ++j) {
-    const int d = lane + 32 * j;
-    nv[j] = p.k_norm ? __fmul_rn(sh[d] / rms, p.k_norm[d]) : sh[d];
-  }
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < HD / 32; ++j) sh[lane + 32 * j] = nv[j];
-  __syncwarp();
-#pragma unroll
-  for (int j = 0; j < HD / 32; ++j) {
-    const int d = lane + 32 * j;
-    float o = nv[j];
-    if (d < p.rd) {
-      const int half = p.rd / 2;
-      int i, other;
-      bool first;
-      if (p.interleaved) {
-        i = d >> 1;
-        first = (d & 1) == 0;
-        other = first ? d + 1 : d - 1;
-      } else if (d < half) {
-        i = d;
-        first = true;
-        other = d + half;
-      } else {
-        i = d - half;
-        first = false;
-        other = d - half;
-      }
-      const int pos_eff = i < p.sec_total ? pos : 0;
-      const float th = rope_angle(i, pos_eff, p.rd, p.rbase, p.freq_scale, p.yarn_on, p.corr_lo,
-                                  p.corr_hi, p.ff, p.use_ff);
-      const float c = __fmul_rn(cosf(th), p.m_scale), sn = __fmul_rn(sinf(th), p.m_scale);
-      const float x1 = first ? nv[j] : sh[other];
-      const float x2 = first ? sh[other] : nv[j];
-      o = first ? __fsub_rn(__fmul_rn(x1, c), __fmul_rn(x2, sn))
-                : __fadd_rn(__fmul_rn(x2, c), __fmul_rn(x1, sn));
-    }
-    Kc[d] = __float2half_rn(o);
-  }
+  for (int d = p.rd + lane; d < HD; d += 32) Kc[d] = __float2half_rn(sh[d]);
   __syncwarp();
 }
 
@@ -419,7 +400,7 @@ __device__ void append_owned_rows(const DecodeParams& p, const int* pref, long u
   }
 }
 
-template <int HD, int HPC, bool Q8, bool FUSE = false>
+template <int HD, int HPC, bool Q8, bool FUSE = false, bool F8 = false>
 __global__ void __launch_bounds__(Geometry<HD, HPC, Q8>::THREADS, 1)
 decode_kernel(const DecodeParams p) {
   using Geo = Geometry<HD, HPC, Q8>;
@@ -675,13 +656,13 @@ decode_kernel(const DecodeParams p) {
 #pragma unroll
             for (int kk = 0; kk < 2; ++kk) {
               const int kt = 2 * blk + kk;
-              const uint32_t w0 = lds_u32(kbase[i] + q_k0 + kt * 16 + 4 * t) ^ 0x80808080u;
-              const uint32_t w1 = lds_u32(kbase[i] + q_k1 + kt * 16 + 4 * t) ^ 0x80808080u;
+              const uint32_t w0 = kv8_bias<F8>(lds_u32(kbase[i] + q_k0 + kt * 16 + 4 * t));
+              const uint32_t w1 = kv8_bias<F8>(lds_u32(kbase[i] + q_k1 + kt * 16 + 4 * t));
               uint32_t a[4];
-              a[0] = i8pair_to_h2(w0, 0x4140);
-              a[1] = i8pair_to_h2(w1, 0x4140);
-              a[2] = i8pair_to_h2(w0, 0x4342);
-              a[3] = i8pair_to_h2(w1, 0x4342);
+              a[0] = kv8_to_h2<F8>(w0, 0x4140);
+              a[1] = kv8_to_h2<F8>(w1, 0x4140);
+              a[2] = kv8_to_h2<F8>(w0, 0x4342);
+              a[3] = kv8_to_h2<F8>(w1, 0x4342);
               mma_16816(sb, a, qlo[kt][0], qlo[kt][1]);
               mma_16816(sb, a, qhi[kt][0], qhi[kt][1]);
             }
@@ -764,23 +745,23 @@ decode_kernel(const DecodeParams p) {
             const uint32_t b0 = movmatrix_trans(pack_half2(pr[i][0] * v0, pr[i][1] * v0));
             const uint32_t b1 = movmatrix_trans(pack_half2(pr[i][2] * v1, pr[i][3] * v1));
             const uint32_t col = vbase[i] + blk * 32 + 4 * g;
-            const uint32_t x0 = lds_u32(col + q_v[0]) ^ 0x80808080u;
-            const uint32_t x1 = lds_u32(col + q_v[1]) ^ 0x80808080u;
-            const uint32_t x2 = lds_u32(col + q_v[2]) ^ 0x80808080u;
-            const uint32_t x3 = lds_u32(col + q_v[3]) ^ 0x80808080u;
+            const uint32_t x0 = kv8_bias<F8>(lds_u32(col + q_v[0]));
+            const uint32_t x1 = kv8_bias<F8>(lds_u32(col + q_v[1]));
+            const uint32_t x2 = kv8_bias<F8>(lds_u32(col + q_v[2]));
+            const uint32_t x3 = kv8_bias<F8>(lds_u32(col + q_v[3]));
             // byte-interleave rows: lo = dims 0,1 of both keys, hi = dims 2,3
             const uint32_t l01 = __byte_perm(x0, x1, 0x5140), h01 = __byte_perm(x0, x1, 0x7362);
             const uint32_t l23 = __byte_perm(x2, x3, 0x5140), h23 = __byte_perm(x2, x3, 0x7362);
             uint32_t a[4];
-            a[0] = i8pair_to_h2(l01, 0x4140);  // dim 4g   (tile 2blk row g),   keys 2t, 2t+1
-            a[1] = i8pair_to_h2(l01, 0x4342);  // dim 4g+1 (tile 2blk row g+8)
-            a[2] = i8pair_to_h2(l23, 0x4140);  // dim 4g,   keys 2t+8, 2t+9
-            a[3] = i8pair_to_h2(l23, 0x4342);
+            a[0] = kv8_to_h2<F8>(l01, 0x4140);  // dim 4g   (tile 2blk row g),   keys 2t, 2t+1
+            a[1] = kv8_to_h2<F8>(l01, 0x4342);  // dim 4g+1 (tile 2blk row g+8)
+            a[2] = kv8_to_h2<F8>(l23, 0x4140);  // dim 4g,   keys 2t+8, 2t+9
+            a[3] = kv8_to_h2<F8>(l23, 0x4342);
             mma_16816(oacc[2 * blk], a, b0, b1);
-            a[0] = i8pair_to_h2(h01, 0x4140);  // dims 4g+2, 4g+3 (tile 2blk+1)
-            a[1] = i8pair_to_h2(h01, 0x4342);
-            a[2] = i8pair_to_h2(h23, 0x4140);
-            a[3] = i8pair_to_h2(h23, 0x4342);
+            a[0] = kv8_to_h2<F8>(h01, 0x4140);  // dims 4g+2, 4g+3 (tile 2blk+1)
+            a[1] = kv8_to_h2<F8>(h01, 0x4342);
+            a[2] = kv8_to_h2<F8>(h23, 0x4140);
+            a[3] = kv8_to_h2<F8>(h23, 0x4342);
             mma_16816(oacc[2 * blk + 1], a, b0, b1);
           }
         }
@@ -1002,11 +983,11 @@ WsLayout ws_layout(int B, int nkv, int hd, int hpc) {
   return w;
 }
 
-template <int HD, int HPC, bool Q8, bool FUSE = false>
+template <int HD, int HPC, bool Q8, bool FUSE = false, bool F8 = false>
 int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st) {
   using Geo = Geometry<HD, HPC, Q8>;
   const size_t smem = (size_t)Geo::STAGES * Geo::STAGE_BYTES + (size_t)(p.B + 1) * sizeof(int);
-  auto kern = decode_kernel<HD, HPC, Q8, FUSE>;
+  auto kern = decode_kernel<HD, HPC, Q8, FUSE, F8>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1050,6 +1031,14 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
 
 template <int HD>
 int launch_decode_hd(DecodeParams& p, long units_hint, int chunk, cudaStream_t st) {
+  if (p.K8 && p.f8) {
+    switch (heads_per_cta(p.nkv, HD, true)) {
+      case 8: return launch_decode_v<HD, (HD <= 128 ? 8 : 4), true, false, true>(p, units_hint, chunk, st);
+      case 4: return launch_decode_v<HD, 4, true, false, true>(p, units_hint, chunk, st);
+      case 2: return launch_decode_v<HD, (HD >= 128 ? 2 : 4), true, false, true>(p, units_hint, chunk, st);
+      default: return launch_decode_v<HD, (HD == 256 ? 1 : 4), true, false, true>(p, units_hint, chunk, st);
+    }
+  }
   if (p.K8) {
     switch (heads_per_cta(p.nkv, HD, true)) {
       case 8: return launch_decode_v<HD, (HD <= 128 ? 8 : 4), true>(p, units_hint, chunk, st);
@@ -1219,8 +1208,10 @@ int decode_fused(const float* q_raw, const float* k_raw, const float* v_raw, con
 int decode_q8(const float* q, const float* gate, const void* const* K8, const void* const* V8,
               const void* const* Ks, const void* const* Vs, const int* pos, const int* max_len,
               float* out, int B, int nq, int nkv, int hd, float scale, int window, float softcap,
-              int max_kv_len, int chunk, void* ws, size_t ws_bytes, cudaStream_t st) {
+              int max_kv_len, int chunk, void* ws, size_t ws_bytes, cudaStream_t st,
+              bool f8 = false) {
   DecodeParams p{};
+  p.f8 = f8 ? 1 : 0;
   p.q = q; p.gate = gate;
   p.K8 = reinterpret_cast<const int8_t* const*>(K8);
   p.V8 = reinterpret_cast<const int8_t* const*>(V8);
@@ -1283,6 +1274,58 @@ int quantize_q8(const float* in, void* q, void* scales, long nblk, cudaStream_t 
   return 0;
 }
 
+// fp8 (e4m3) quantiser for the 8-bit cache layout of the Q8_0 path: each
+// 32-value block gets s = fp16(max|v| / 448) and values e4m3(v / s) rounded
+// to nearest even with saturation to +-448 (cvt.rn.satfinite); a block whose
+// scale is 0 gets zeros. A value reads back as e4m3 x s. No counterpart in
+// the reference (its 8-bit KV mode is Q8_0); same storage geometry.
+__global__ void quantize_fp8_kernel(const float* __restrict__ in, uint8_t* __restrict__ q,
+                                    __half* __restrict__ sc, long nblk) {
+  const long b = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= nblk) return;
+  const float4* v4 = reinterpret_cast<const float4*>(in + b * 32);
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float4 t = v4[i];
+    v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  const __half sh = __float2half_rn(__fdiv_rn(amax, 448.f));
+  sc[b] = sh;
+  const float s = __half2float(sh);
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint32_t x = 0;
+#pragma unroll
+    for (int k = 0; k < 4; k += 2) {
+      float2 f = make_float2(0.f, 0.f);
+      if (s > 0.f) f = make_float2(__fdiv_rn(v[4 * i + k], s), __fdiv_rn(v[4 * i + k + 1], s));
+      const __nv_fp8x2_storage_t pr = __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
+      x |= (uint32_t)pr << (8 * k);
+    }
+    w[i] = x;
+  }
+  uint4* qo = reinterpret_cast<uint4*>(q + b * 32);
+  qo[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  qo[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+int quantize_fp8(const float* in, void* q, void* scales, long nblk, cudaStream_t st) {
+  if (nblk < 0 || (nblk > 0 && (!in || !q || !scales))) return record_status(ASPIDA_ERR_ARG);
+  if (((uintptr_t)in & 15) || ((uintptr_t)q & 15) || ((uintptr_t)scales & 1))
+    return record_status(ASPIDA_ERR_ARG);
+  if (nblk == 0) return 0;
+  const int threads = 128;
+  quantize_fp8_kernel<<<(unsigned)((nblk + threads - 1) / threads), threads, 0, st>>>(
+      in, static_cast<uint8_t*>(q), static_cast<__half*>(scales), nblk);
+  ASPIDA_CHECK_LAUNCH();
+  return 0;
+}
+
 }  // namespace aspida
 
 extern "C" int aspida_attn_decode_q8(const float* q, const float* gate, const void* const* K8,
@@ -1315,6 +1358,23 @@ extern "C" int aspida_attn_decode_fused(
 extern "C" int aspida_attn_quantize_q8(const float* in, void* q, void* scales, long long nblk,
                                        void* stream) {
   return aspida::quantize_q8(in, q, scales, (long)nblk, (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_quantize_fp8(const float* in, void* q, void* scales, long long nblk,
+                                        void* stream) {
+  return aspida::quantize_fp8(in, q, scales, (long)nblk, (cudaStream_t)stream);
+}
+
+extern "C" int aspida_attn_decode_fp8(const float* q, const float* gate, const void* const* K8,
+                                      const void* const* V8, const void* const* K_scales,
+                                      const void* const* V_scales, const int* pos,
+                                      const int* max_len, float* out, int B, int nq, int nkv,
+                                      int hd, float scale, int window, float softcap,
+                                      int max_kv_len, int chunk, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  return aspida::decode_q8(q, gate, K8, V8, K_scales, V_scales, pos, max_len, out, B, nq, nkv,
+                           hd, scale, window, softcap, max_kv_len, chunk, workspace,
+                           workspace_bytes, (cudaStream_t)stream, true);
 }
 
 extern "C" size_t aspida_attn_decode_workspace_size(int B, int nq, int nkv, int hd,

@@ -51,7 +51,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", action="store_true",
                     help="for ncu: only warm-up + timed steps of one leg, no clock soak, e2e or CPU")
-    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long", "q8", "cfg4"], default="decode")
+    ap.add_argument("--profile-leg", choices=["decode", "prefill", "long", "q8", "fp8", "cfg4"],
+                    default="decode")
     return ap.parse_args()
 
 
@@ -259,17 +260,18 @@ def long_leg(ab, torch, dev, rank, world, steps, warmup, stream, dist):
     return e0.elapsed_time(e1) / steps, n * nkv * hd * 2 * 2, transport
 
 
-def q8_leg(ab, torch, dev, lens, steps, warmup, stream, seed):
+def q8_leg(ab, torch, dev, lens, steps, warmup, stream, seed, fp8=False):
     """Config-2 batch on Q8_0 caches (int8 + fp16 scale per 32 values, the
-    reference's KVMODE 2 storage), quantised on the device from seeded N(0,1)
-    f32. Returns (ms per step, algorithmic bytes per step)."""
+    reference's KVMODE 2 storage) or, with fp8, on fp8 e4m3 caches of the same
+    geometry, quantised on the device from seeded N(0,1) f32. Returns (ms per
+    step, algorithmic bytes per step)."""
     g = torch.Generator(device=dev).manual_seed(seed)
     kvd = NKV * HD
     K8, V8, Ks, Vs = [], [], [], []
     for L in lens:
         for dst8, dsts in ((K8, Ks), (V8, Vs)):
             x = torch.randn(L, kvd, generator=g, device=dev)
-            a, s = ab.quantize_q8(x)
+            a, s = ab.quantize_fp8(x) if fp8 else ab.quantize_q8(x)
             dst8.append(a)
             dsts.append(s)
             del x
@@ -280,9 +282,10 @@ def q8_leg(ab, torch, dev, lens, steps, warmup, stream, seed):
     ws = ab.Workspace()
     maxkv = max(lens)
 
+    dec = ab.decode_fp8 if fp8 else ab.decode_q8
+
     def step():
-        ab.decode_q8(q, *tabs, pos, NQ, NKV, HD, max_kv_len=maxkv, out=out, workspace=ws,
-                     stream=stream)
+        dec(q, *tabs, pos, NQ, NKV, HD, max_kv_len=maxkv, out=out, workspace=ws, stream=stream)
 
     for _ in range(max(3, warmup)):
         step()
@@ -506,10 +509,11 @@ def main():
             for c in caches:
                 c.free()
             cfg4_legs(ab, torch, dev, args.steps, args.warmup, stream, 5000 + rank)
-        elif args.profile_leg == "q8":
+        elif args.profile_leg in ("q8", "fp8"):
             for c in caches:
                 c.free()
-            q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4000 + rank)
+            q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4000 + rank,
+                   fp8=args.profile_leg == "fp8")
         elif args.profile_leg == "prefill":
             for c in caches:
                 c.free()
@@ -580,8 +584,11 @@ def main():
                                           dist)
     torch.cuda.empty_cache()
     q_ms, q_bytes = q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4000 + rank)
+    torch.cuda.empty_cache()
+    f_ms, f_bytes = q8_leg(ab, torch, dev, lens, args.steps, args.warmup, stream, 4500 + rank,
+                           fp8=True)
     if ab.device_status() != 0:
-        raise RuntimeError("device status after q8 decode")
+        raise RuntimeError("device status after q8 / fp8 decode")
     torch.cuda.empty_cache()
     x_steps = max(5, min(args.steps, 20))
     c4 = cfg4_legs(ab, torch, dev, x_steps, args.warmup, stream, 5000 + rank)
@@ -592,9 +599,9 @@ def main():
         raise RuntimeError("device status after cfg4 / cfg5b")
 
     nbytes = algo_bytes(lens)
-    times = [ms, ms_e2e, p_ms, l_ms, q_ms, c4["prefill_ms"], c4["decode_ms"], b_ms]
+    times = [ms, ms_e2e, p_ms, l_ms, q_ms, c4["prefill_ms"], c4["decode_ms"], b_ms, f_ms]
     work = [float(nbytes), float(p_flops), float(l_bytes), float(q_bytes),
-            float(c4["prefill_flops"]), float(c4["decode_bytes"]), float(b_bytes)]
+            float(c4["prefill_flops"]), float(c4["decode_bytes"]), float(b_bytes), float(f_bytes)]
     stats = torch.tensor(times + work, dtype=torch.float64, device=dev)
     if dist:
         mx = stats[:len(times)].clone()
@@ -604,8 +611,9 @@ def main():
         times_max, work_all = [float(x) for x in mx], [float(x) for x in tot]
     else:
         times_max, work_all = times, work
-    ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max, c4p_max, c4d_max, b_ms_max = times_max
-    bytes_all, flops_all, l_bytes_all, q_bytes_all, c4p_all, c4d_all, b_all = work_all
+    ms_max, ms_e2e_max, p_ms_max, l_ms_max, q_ms_max, c4p_max, c4d_max, b_ms_max, f_ms_max = \
+        times_max
+    bytes_all, flops_all, l_bytes_all, q_bytes_all, c4p_all, c4d_all, b_all, f_bytes_all = work_all
 
     if rank == 0:
         hbm, src = peaks()
@@ -669,6 +677,19 @@ def main():
                          "peak": peaks()[0], "unit": "GB/s",
                          "frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks()[0], 4),
                          "traffic": traffic("decode_q8_cfg2")},
+            "gpu_launches": args.steps * 2,
+        }
+        line["decode_fp8"] = {
+            "metric": "decode attn KV GB/s over fp8 e4m3 caches (cfg2 lengths and heads, e4m3 + "
+                      "fp16 scale per 32 values)",
+            "value": round(f_bytes_all / (f_ms_max * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(f_ms_max, 5),
+            "speedup_vs_fp16_kv": round(ms_max / f_ms_max, 3),
+            "bytes_per_step_per_gpu": int(f_bytes),
+            "roofline": {"bound": "hbm", "achieved": round(f_bytes / (f_ms * 1e-3) / 1e9, 1),
+                         "peak": peaks()[0], "unit": "GB/s",
+                         "frac": round(f_bytes / (f_ms * 1e-3) / 1e9 / peaks()[0], 4),
+                         "traffic": traffic("decode_fp8_cfg2")},
             "gpu_launches": args.steps * 2,
         }
         hbm_peak, tc_peak = peaks()[0], peaks_tensor()[0]

@@ -228,6 +228,28 @@ int aspida_attn_decode_q8(const float* q, const float* gate, const void* const* 
                           float softcap, int max_kv_len, int chunk, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* Decode over fp8 (e4m3) KV caches, the fp8 half of the 8-bit KV modes
+ * (the reference's 8-bit mode is Q8_0, gpu/fattn_kvhalf.cu:55-152; fp8 has no
+ * counterpart there). Same storage geometry and table convention as
+ * aspida_attn_decode_q8: K8 / V8 tables of uint8 e4m3 code caches
+ * [rows][nkv*hd], K_scales / V_scales tables of fp16 scales [rows][nkv*hd/32]
+ * (one per 32-value block along a row); value = e4m3(code) * scale, which
+ * aspida_attn_quantize_fp8 writes. Other arguments, the workspace and the
+ * supported shapes as aspida_attn_decode_q8. */
+int aspida_attn_decode_fp8(const float* q, const float* gate, const void* const* K8,
+                           const void* const* V8, const void* const* K_scales,
+                           const void* const* V_scales, const int* pos, const int* max_len,
+                           float* out, int B, int nq, int nkv, int hd, float scale, int window,
+                           float softcap, int max_kv_len, int chunk, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* fp8 (e4m3) quantiser for aspida_attn_decode_fp8's caches: nblk blocks of 32
+ * consecutive f32 values; scales[b] = fp16(max|v| / 448); code =
+ * e4m3(v / float(scales[b])), round to nearest even, saturating at +-448;
+ * a block with scale 0 gets zeros. in and q 16-byte aligned. */
+int aspida_attn_quantize_fp8(const float* in, void* q, void* scales, long long nblk,
+                             void* stream);
+
 /* Gated causal prefill over Q8_0 caches with the argument meaning of the
  * reference's k_gqa_kv<..., 2> (gpu/fattn_kvhalf.cu:59-130, launched at
  * 162-190): q_all / gate f32 [P][nq*hd] (q 16-byte aligned), K8 / V8 int8

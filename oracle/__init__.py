@@ -186,3 +186,59 @@ def dequantize_q8(q, scales):
     q = np.asarray(q)
     s = np.asarray(scales).astype(np.float32)
     return (q.astype(np.float32).reshape(-1, 32) * s.reshape(-1, 1)).reshape(q.shape)
+
+
+def _e4m3_table():
+    """Values of the 127 non-negative finite e4m3 codes 0x00..0x7e (OCP FP8
+    E4M3: 4 exponent bits, bias 7, 3 mantissa bits, subnormals, no infinity;
+    0x7f is NaN)."""
+    vals = np.empty(127, np.float64)
+    for c in range(127):
+        e, m = c >> 3, c & 7
+        vals[c] = (m / 8.0) * 2.0 ** -6 if e == 0 else (1.0 + m / 8.0) * 2.0 ** (e - 7)
+    return vals
+
+
+_E4M3 = _e4m3_table()
+
+
+def e4m3_encode(x):
+    """f32 -> e4m3 codes (uint8): round to nearest, ties to the even code,
+    saturating at +-448 (cvt.rn.satfinite.e4m3x2.f32 semantics)."""
+    x = np.asarray(x, np.float32).astype(np.float64)
+    a = np.minimum(np.abs(x), 448.0)
+    hi = np.clip(np.searchsorted(_E4M3, a, side="left"), 0, 126)
+    lo = np.clip(hi - 1, 0, 126)
+    dlo, dhi = a - _E4M3[lo], _E4M3[hi] - a
+    pick_hi = (dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0))
+    code = np.where(pick_hi, hi, lo).astype(np.uint8)
+    return np.where(np.signbit(x) & (code != 0), code | 0x80, code).astype(np.uint8)
+
+
+def e4m3_decode(codes):
+    c = np.asarray(codes, np.uint8)
+    v = _E4M3[np.minimum(c & 0x7F, 126)].astype(np.float32)
+    return np.where(c & 0x80, -v, v).astype(np.float32)
+
+
+def quantize_fp8(x):
+    """fp8 (e4m3) block quantisation of aspida_attn_quantize_fp8, in numpy: per
+    32-value block s = fp16(max|v| / 448) (f32 division), code = e4m3(v / s)
+    (f32 division, nearest-even, saturating), zeros when s = 0. Returns
+    (uint8 codes, fp16 scales)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    blocks = x.reshape(-1, 32)
+    amax = np.max(np.abs(blocks), axis=1)
+    s16 = (amax / np.float32(448)).astype(np.float32).astype(np.float16)
+    s = s16.astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        y = np.where(s[:, None] > 0, blocks / s[:, None], np.float32(0)).astype(np.float32)
+    codes = e4m3_encode(y)
+    return codes.reshape(x.shape), s16.reshape(*x.shape[:-1], x.shape[-1] // 32)
+
+
+def dequantize_fp8(codes, scales):
+    """Values the fp8 decode reads: float(e4m3 code) * float(fp16 scale), f32."""
+    v = e4m3_decode(codes).reshape(-1, 32)
+    s = np.asarray(scales).astype(np.float32).reshape(-1, 1)
+    return (v * s).reshape(np.asarray(codes).shape)

@@ -219,6 +219,44 @@ def test_step_host_matches_oracle(ab, oracle, rd):
         c.free()
 
 
+def test_step_host_two_chunks_matches_oracle(ab, oracle):
+    """A batch of 16+ sequences runs as two chunks on two streams (the second
+    chunk's copies under the first chunk's decode); odd B splits 8 + 9.
+    Two calls in a row (the second reuses the staging and the aux stream)."""
+    nq, nkv, hd = 32, 8, 128
+    rng = np.random.RandomState(18)
+    lens = rng.randint(1, 3000, size=17).tolist()
+    caches = [ab.KVCache(L + 8, nkv, hd, nq) for L in lens]
+    Kf, Vf = [], []
+    for c, L in zip(caches, lens):
+        kr = rng.standard_normal((L, nkv * hd)).astype(np.float32)
+        vr = rng.standard_normal((L, nkv * hd)).astype(np.float32)
+        c.K[:L] = torch.from_numpy(kr).half().cuda()
+        c.V[:L] = torch.from_numpy(vr).half().cuda()
+        Kf.append(kr.astype(np.float16).astype(np.float32))
+        Vf.append(vr.astype(np.float16).astype(np.float32))
+    B = len(lens)
+    for step in range(2):
+        pos = [L + step for L in lens]
+        q = torch.from_numpy(rng.standard_normal((B, nq * hd)).astype(np.float32)).pin_memory()
+        k = torch.from_numpy(rng.standard_normal((B, nkv * hd)).astype(np.float32)).pin_memory()
+        v = torch.from_numpy(rng.standard_normal((B, nkv * hd)).astype(np.float32)).pin_memory()
+        out = torch.empty(B, nq * hd).pin_memory()
+        ab.step_host([c.handle for c in caches], q, k, v, pos, out, nq, nkv, hd,
+                     rope_dim=hd, rope_base=500000.0)
+        qr = np.stack([oracle.rope_rows(q[b:b + 1].numpy(), nq, hd, [pos[b]], 500000.0)[0]
+                       for b in range(B)])
+        for b in range(B):
+            kr = oracle.rope_rows(k[b:b + 1].numpy(), nkv, hd, [pos[b]], 500000.0)[0]
+            Kf[b] = np.concatenate([Kf[b], kr.astype(np.float16).astype(np.float32)[None]])
+            Vf[b] = np.concatenate([Vf[b], v[b:b + 1].numpy().astype(np.float16).astype(np.float32)])
+        ref = oracle.decode_batch(qr, Kf, Vf, pos, nq, nkv, hd)
+        assert_parity(out.numpy(), ref, what=f"step_host two chunks, call {step}")
+    assert ab.device_status() == 0
+    for c in caches:
+        c.free()
+
+
 def test_argument_errors(ab):
     q = torch.zeros(1, 32 * 96, device="cuda")
     t = torch.zeros(1, dtype=torch.int64, device="cuda")
