@@ -160,10 +160,25 @@ __device__ __forceinline__ void warp_norm_row(const float* __restrict__ x,
                                               const float* __restrict__ w, float eps, int hd,
                                               float* sh, int lane) {
   float ss = 0.f;
-  for (int d = lane; d < hd; d += 32) {
-    const float v = x[d];
-    sh[d] = v;
-    ss = __fadd_rn(ss, __fmul_rn(v, v));
+  if (hd <= 256) {
+    // every load issued before any is used: one memory round trip per row,
+    // which matters when x is pinned host memory read over PCIe
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = lane + 32 * j < hd ? x[lane + 32 * j] : 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (lane + 32 * j < hd) {
+        sh[lane + 32 * j] = v[j];
+        ss = __fadd_rn(ss, __fmul_rn(v[j], v[j]));
+      }
+    }
+  } else {
+    for (int d = lane; d < hd; d += 32) {
+      const float v = x[d];
+      sh[d] = v;
+      ss = __fadd_rn(ss, __fmul_rn(v, v));
+    }
   }
   if (w) {
 #pragma unroll

@@ -68,7 +68,16 @@ __global__ void __launch_bounds__(kPrepWarps * 32) prep_kernel(const PrepArgs a)
   if (!is_q) {
     const float* vr = a.v + t * kvd + (long)kvh * hd;
     __half* vd = Vc + crow * kvd + (long)kvh * hd;
-    for (int d = lane; d < hd; d += 32) vd[d] = __float2half_rn(vr[d]);
+    if (hd <= 256) {
+      float t[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) t[j] = lane + 32 * j < hd ? vr[lane + 32 * j] : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (lane + 32 * j < hd) vd[lane + 32 * j] = __float2half_rn(t[j]);
+    } else {
+      for (int d = lane; d < hd; d += 32) vd[d] = __float2half_rn(vr[d]);
+    }
   }
   warp_norm_row(x, is_q ? a.q_norm : a.k_norm, a.eps, hd, sh, lane);
   float* qf = nullptr;

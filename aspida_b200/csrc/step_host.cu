@@ -3,13 +3,13 @@
 // (gpu/gpu_matvec.cu:1613-1666, 2783-2894) without the projections.
 //
 // Per call: one H2D of the lane descriptors (positions, bounds, K/V table),
-// then, per chunk of the batch, H2D of its q/k/v, the batched prep (RoPE +
-// fp16 K/V append at pos[b]), the split-KV decode and the D2H of its output;
-// finally a stream synchronise. A batch of 16 or more sequences runs as two
-// chunks on two streams (the caller's and a library-owned one), so the second
-// chunk's host-to-device copies run under the first chunk's decode and the
-// first chunk's output copy under the second's: the PCIe transfers, which at
-// config 2 are a third of the step, mostly leave the critical path.
+// H2D of q/k/v, the batched prep (RoPE + fp16 K/V append at pos[b]), the
+// split-KV decode, and a stream synchronise. Buffers in pinned host memory
+// that the device can address (cudaMallocHost / cudaHostRegister) are used in
+// place over PCIe: the prep kernel reads pinned q/k/v directly (no H2D copy
+// calls, every row's loads in flight at once), and the decode writes a pinned
+// `out` directly while other CTAs are still streaming the cache (no D2H copy
+// after it). Pageable buffers go through device staging with one copy each.
 // Device staging is cached per (device, stream) and grown on demand, so calls
 // on different streams do not share scratch.
 #include <map>
@@ -42,8 +42,6 @@ struct Staging {
   void* pinned = nullptr;    // lane descriptors, host side
   size_t pinned_bytes = 0;
   bool pending = false;      // copies from `pinned` may still be in flight
-  cudaStream_t aux = nullptr;          // second stream for the second chunk
-  cudaEvent_t ev_desc = nullptr, ev_done = nullptr;
 };
 
 std::mutex g_stage_mu;
@@ -78,20 +76,11 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
     max_kv = std::max(max_kv, pos[b] + 1);
   }
 
-  const int nch = B >= 16 ? 2 : 1;                       // batch chunks
-  const int Bc[2] = {nch == 2 ? B / 2 : B, nch == 2 ? B - B / 2 : 0};
-  int mkv[2] = {1, 1};
-  for (int b = 0; b < B; ++b) {
-    const int c = b < Bc[0] ? 0 : 1;
-    mkv[c] = std::max(mkv[c], pos[b] + 1);
-  }
-  (void)max_kv;
   const size_t desc_bytes = al256((size_t)B * (2 * sizeof(int) + 2 * sizeof(void*)));
   const size_t qb = al256((size_t)B * nq * hd * sizeof(float));
   const size_t kb = al256((size_t)B * kvd * sizeof(float));
-  size_t wsz[2] = {0, 0};
-  for (int c = 0; c < nch; ++c) wsz[c] = al256(decode_workspace_size(Bc[c], nq, nkv, hd, mkv[c], 0));
-  const size_t need = desc_bytes + 3 * qb + 2 * kb + wsz[0] + wsz[1];  // q, q_roped, out, k, v, ws
+  const size_t ws = al256(decode_workspace_size(B, nq, nkv, hd, max_kv, 0));
+  const size_t need = desc_bytes + 3 * qb + 2 * kb + ws;  // q, q_roped, out, k, v, ws
 
   int dev = 0;
   cudaGetDevice(&dev);
@@ -107,20 +96,11 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
     if (cudaMallocHost(&s.pinned, desc_bytes) != cudaSuccess) return record_status(ASPIDA_ERR_NOMEM);
     s.pinned_bytes = desc_bytes;
   }
-  if (nch == 2 && !s.aux) {
-    if (cudaStreamCreateWithFlags(&s.aux, cudaStreamNonBlocking) != cudaSuccess ||
-        cudaEventCreateWithFlags(&s.ev_desc, cudaEventDisableTiming) != cudaSuccess ||
-        cudaEventCreateWithFlags(&s.ev_done, cudaEventDisableTiming) != cudaSuccess) {
-      cudaGetLastError();
-      return record_status(ASPIDA_ERR_NOMEM);
-    }
-  }
   // The pinned descriptor block is reused by the next call on this stream:
   // a call that returned early may have left its H2D in flight (a complete
   // call ends with a synchronisation, so there is nothing to wait for).
   if (s.pending) {
     cudaStreamSynchronize(st);
-    if (s.aux) cudaStreamSynchronize(s.aux);
     s.pending = false;
   }
 
@@ -141,48 +121,53 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
   float* dout = reinterpret_cast<float*>(d + desc_bytes + 2 * qb);
   float* dk = reinterpret_cast<float*>(d + desc_bytes + 3 * qb);
   float* dv = reinterpret_cast<float*>(d + desc_bytes + 3 * qb + kb);
-  unsigned char* dws = d + desc_bytes + 3 * qb + 2 * kb;
+  void* dws = d + desc_bytes + 3 * qb + 2 * kb;
 
-  const long qrow = (long)nq * hd;
+  const size_t qbytes = (size_t)B * nq * hd * sizeof(float), kbytes = (size_t)B * kvd * sizeof(float);
+  // device address of a pinned host buffer, or null (pageable / unknown memory)
+  auto mapped = [](const void* h) -> void* {
+    cudaPointerAttributes pa;
+    if (cudaPointerGetAttributes(&pa, h) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    return pa.type == cudaMemoryTypeHost ? pa.devicePointer : nullptr;
+  };
+  float* out_direct = static_cast<float*>(mapped(out));
+#ifndef ASPIDA_STEP_NO_ZC_IN
+  const float* qd = static_cast<const float*>(mapped(q));
+  const float* kd = static_cast<const float*>(mapped(k));
+  const float* vd = static_cast<const float*>(mapped(v));
+  if (!qd || !kd || !vd) qd = kd = vd = nullptr;
+#endif
   int rc = 0;
   s.pending = true;
   if ((rc = cuda_status(cudaMemcpyAsync(d, hp, desc_bytes, cudaMemcpyHostToDevice, st)))) return rc;
-  if (nch == 2) {
-    if ((rc = cuda_status(cudaEventRecord(s.ev_desc, st)))) return rc;
-    if ((rc = cuda_status(cudaStreamWaitEvent(s.aux, s.ev_desc, 0)))) return rc;
+#ifndef ASPIDA_STEP_NO_ZC_IN
+  if (qd) {
+    dq = const_cast<float*>(qd);
+    dk = const_cast<float*>(kd);
+    dv = const_cast<float*>(vd);
+  } else
+#endif
+  {
+    if ((rc = cuda_status(cudaMemcpyAsync(dq, q, qbytes, cudaMemcpyHostToDevice, st)))) return rc;
+    if ((rc = cuda_status(cudaMemcpyAsync(dk, k, kbytes, cudaMemcpyHostToDevice, st)))) return rc;
+    if ((rc = cuda_status(cudaMemcpyAsync(dv, v, kbytes, cudaMemcpyHostToDevice, st)))) return rc;
   }
-  for (int c = 0, b0 = 0; c < nch; b0 += Bc[c], ++c) {
-    cudaStream_t cs = c == 0 ? st : s.aux;
-    const int n = Bc[c];
-    const size_t qbytes = (size_t)n * qrow * sizeof(float), kbytes = (size_t)n * kvd * sizeof(float);
-    float* cq = dq + b0 * qrow;
-    float* cqr = dqr + b0 * qrow;
-    float* cout = dout + b0 * qrow;
-    float* ck = dk + (long)b0 * kvd;
-    float* cv = dv + (long)b0 * kvd;
-    if ((rc = cuda_status(cudaMemcpyAsync(cq, q + b0 * qrow, qbytes, cudaMemcpyHostToDevice, cs))))
-      return rc;
-    if ((rc = cuda_status(cudaMemcpyAsync(ck, k + (long)b0 * kvd, kbytes, cudaMemcpyHostToDevice, cs))))
-      return rc;
-    if ((rc = cuda_status(cudaMemcpyAsync(cv, v + (long)b0 * kvd, kbytes, cudaMemcpyHostToDevice, cs))))
-      return rc;
-    // prep, then decode: measured faster on B200 than the single-launch
-    // aspida_attn_decode_fused (config 2: 0.137 vs ~0.107 ms)
-    if ((rc = launch_prep_lanes(cq, ck, cv, n, nq, nkv, hd, cqr, dK + b0, dV + b0, dpos + b0,
-                                dml + b0, rd, base, interleaved, cs)))
-      return rc;
-    if ((rc = decode(cqr, nullptr, reinterpret_cast<const void* const*>(dK + b0),
-                     reinterpret_cast<const void* const*>(dV + b0), dpos + b0, dml + b0, cout, n,
-                     nq, nkv, hd, scale, window, softcap, mkv[c], 0, dws + (c ? wsz[0] : 0),
-                     wsz[c], cs)))
-      return rc;
-    if ((rc = cuda_status(cudaMemcpyAsync(out + b0 * qrow, cout, qbytes, cudaMemcpyDeviceToHost, cs))))
-      return rc;
-  }
-  if (nch == 2) {
-    if ((rc = cuda_status(cudaEventRecord(s.ev_done, s.aux)))) return rc;
-    if ((rc = cuda_status(cudaStreamWaitEvent(st, s.ev_done, 0)))) return rc;
-  }
+  // prep, then decode: measured faster on B200 than the single-launch
+  // aspida_attn_decode_fused (config 2: 0.137 vs ~0.107 ms)
+  if ((rc = launch_prep_lanes(dq, dk, dv, B, nq, nkv, hd, dqr, dK, dV, dpos, dml, rd, base,
+                              interleaved, st)))
+    return rc;
+  if ((rc = decode(dqr, nullptr, reinterpret_cast<const void* const*>(dK),
+                   reinterpret_cast<const void* const*>(dV), dpos, dml,
+                   out_direct ? out_direct : dout, B, nq, nkv, hd, scale, window, softcap, max_kv,
+                   0, dws, ws, st)))
+    return rc;
+  if (!out_direct &&
+      (rc = cuda_status(cudaMemcpyAsync(out, dout, qbytes, cudaMemcpyDeviceToHost, st))))
+    return rc;
   rc = cuda_status(cudaStreamSynchronize(st));
   if (rc == 0) s.pending = false;
   return rc;

@@ -204,7 +204,8 @@ _E4M3 = _e4m3_table()
 
 def e4m3_encode(x):
     """f32 -> e4m3 codes (uint8): round to nearest, ties to the even code,
-    saturating at +-448 (cvt.rn.satfinite.e4m3x2.f32 semantics)."""
+    saturating at +-448, the sign kept (a negative value that rounds to zero
+    gives -0, 0x80) - cvt.rn.satfinite.e4m3x2.f32 semantics."""
     x = np.asarray(x, np.float32).astype(np.float64)
     a = np.minimum(np.abs(x), 448.0)
     hi = np.clip(np.searchsorted(_E4M3, a, side="left"), 0, 126)
@@ -212,7 +213,7 @@ def e4m3_encode(x):
     dlo, dhi = a - _E4M3[lo], _E4M3[hi] - a
     pick_hi = (dhi < dlo) | ((dhi == dlo) & (hi % 2 == 0))
     code = np.where(pick_hi, hi, lo).astype(np.uint8)
-    return np.where(np.signbit(x) & (code != 0), code | 0x80, code).astype(np.uint8)
+    return np.where(np.signbit(x), code | 0x80, code).astype(np.uint8)
 
 
 def e4m3_decode(codes):

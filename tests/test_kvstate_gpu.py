@@ -15,6 +15,7 @@ def ab():
 
 
 def test_new_free_reuse(ab):
+    ab.last_error()                       # a status latched by an earlier test
     h1 = ab.fattn_new(128, 1024, 32)
     h2 = ab.fattn_new(64, 1024, 32)
     assert h1 >= 0 and h2 >= 0 and h1 != h2

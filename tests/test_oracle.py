@@ -246,16 +246,18 @@ def test_window_and_softcap_definitions(oracle):
 def test_e4m3_codec_known_answers(oracle):
     """The numpy e4m3 codec (the fp8 KV oracle) against the OCP FP8 E4M3
     encoding: exact values, the largest finite value, saturation, the
-    smallest normal and subnormal, ties to the even code, signed zero."""
+    smallest normal and subnormal, ties to the even code, signed zero (a
+    negative value that rounds to zero keeps its sign, as cvt does)."""
     cases = {1.0: 0x38, 0.5: 0x30, -2.0: 0xC0, 448.0: 0x7E, 1000.0: 0x7E, -1e9: 0xFE,
              2.0 ** -6: 0x08, 2.0 ** -9: 0x01, 0.875 * 2.0 ** -6: 0x07, 1.0625: 0x38,
-             1.1875: 0x3A, 2.0 ** -10: 0x00, 3 * 2.0 ** -10: 0x02, 0.0: 0x00, 240.0: 0x77}
+             1.1875: 0x3A, 2.0 ** -10: 0x00, 3 * 2.0 ** -10: 0x02, 0.0: 0x00, 240.0: 0x77,
+             -2.0 ** -11: 0x80}
     got = oracle.e4m3_encode(np.array(list(cases), np.float32))
     assert list(got) == list(cases.values())
     codes = np.arange(256, dtype=np.uint8)
     codes = codes[(codes & 0x7F) != 0x7F]                       # drop the NaN codes
     back = oracle.e4m3_encode(oracle.e4m3_decode(codes))
-    assert np.array_equal(back[codes != 0x80], codes[codes != 0x80])  # -0 encodes as +0
+    assert np.array_equal(back, codes)
 
 
 def test_fp8_block_quantiser_round_trip(oracle):
