@@ -185,3 +185,28 @@ def test_prefill_hd128_short_chunk_one_tile(ab, oracle, P, ps, out_dtype):
     ref = oracle.prefill(q.float().cpu().numpy(), K.float().cpu().numpy(),
                          V.float().cpu().numpy(), ps, nq, nkv, hd, rows=rows)
     assert_parity(out.float().cpu().numpy()[rows], ref[rows], what=f"hd128 one-tile P={P}")
+
+
+@pytest.mark.parametrize("qscale", [2.0, 4.0])
+def test_gated_prefill_larger_queries(ab, oracle, qscale):
+    """The gated path rounds the shim's f32 queries to fp16 before the score
+    MMA (the decode keeps an fp16 hi + lo pair). At the hura dims this holds
+    the tolerance for queries up to 4x N(0,1) (score std 4 at scale 1/16);
+    at 8x the rounding of q moves peaked softmaxes by ~4e-3."""
+    from aspida_b200 import _lib
+    nq, nkv, hd, P, ps = 16, 2, 256, 256, 1000
+    g = torch.Generator(device="cuda").manual_seed(int(qscale) + 90)
+    q = torch.randn(P, nq * hd, generator=g, device="cuda") * qscale
+    K = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    V = torch.randn(ps + P, nkv * hd, generator=g, device="cuda").half()
+    gate = torch.randn(P, nq * hd, generator=g, device="cuda")
+    out = torch.full((P, nq * hd), float("nan"), device="cuda")
+    rc = _lib.load().aspida_attn_prefill_gated(q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                               gate.data_ptr(), out.data_ptr(), nq, nkv, hd, P,
+                                               ps, torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    rows = [0, 1, 100, 200, 255]
+    ref = oracle.prefill(q.cpu().numpy(), K.float().cpu().numpy(), V.float().cpu().numpy(), ps,
+                         nq, nkv, hd, gate=gate.cpu().numpy(), rows=rows)
+    assert_parity(out.cpu().numpy()[rows], ref[rows], what=f"gated prefill q x{qscale}")
