@@ -15,6 +15,7 @@ unknown handle).
 """
 from __future__ import annotations
 
+import array
 import ctypes as C
 import math
 from dataclasses import dataclass, field
@@ -434,6 +435,20 @@ def merge(m: torch.Tensor, l: torch.Tensor, o: torch.Tensor,
     return out
 
 
+def _int32_host(xs):
+    """A host int32 array for an ABI argument: (object to keep alive, address).
+    Accepts a CPU int32 tensor or an array.array('i') as is; otherwise builds
+    an array.array (a few microseconds for a batch, where a ctypes array of
+    Python ints costs several times that on every decode step)."""
+    if isinstance(xs, torch.Tensor):
+        if xs.dtype != torch.int32 or xs.is_cuda or not xs.is_contiguous():
+            xs = xs.to(device="cpu", dtype=torch.int32).contiguous()
+        return xs, xs.data_ptr()
+    if not (isinstance(xs, array.array) and xs.typecode == "i"):
+        xs = array.array("i", xs)
+    return xs, xs.buffer_info()[0]
+
+
 def step_host(handles: Sequence[int], q, k, v, pos, out, nq: int, nkv: int, hd: int, *,
               scale: Optional[float] = None, window: int = 0, softcap: float = 0.0,
               rope_dim: int = 0, rope_base: float = 10000.0, interleaved: bool = False,
@@ -442,18 +457,13 @@ def step_host(handles: Sequence[int], q, k, v, pos, out, nq: int, nkv: int, hd: 
     B = len(handles)
     if scale is None:
         scale = 1.0 / math.sqrt(hd)
-    h = (C.c_int * B)(*handles)
-    pos_arr = None
-    if isinstance(pos, torch.Tensor):
-        p = pos.data_ptr()
-    else:
-        pos_arr = (C.c_int * B)(*pos)
-        p = C.addressof(pos_arr)
+    h, hp = _int32_host(handles)
+    pa, pp = _int32_host(pos)
     rc = _lib_().aspida_attn_step_host(
-        C.cast(h, C.c_void_p), B, q.data_ptr(), k.data_ptr(), v.data_ptr(), p, out.data_ptr(),
+        hp, B, q.data_ptr(), k.data_ptr(), v.data_ptr(), pp, out.data_ptr(),
         nq, nkv, hd, scale, window, softcap, rope_dim, rope_base, int(interleaved),
         _stream(stream))
-    del pos_arr
+    del h, pa
     _check(rc, "step_host")
 
 
