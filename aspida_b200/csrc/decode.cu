@@ -65,6 +65,7 @@ struct DecodeParams {
   const __half* const* Ks;    // ... and fp16 scales [rows][nkv*hd/32]
   const __half* const* Vs;
   int f8;                     // the 8-bit caches hold fp8 e4m3 values, not int8
+  int pdl;                    // launched as a programmatic dependent of the prep kernel
   const __half* Kpool;  // paged form: shared pools of blocks of block_size rows
   const __half* Vpool;
   const int* block_table;   // [B][max_blocks] block ids, or null (per-sequence caches)
@@ -461,9 +462,17 @@ decode_kernel(const DecodeParams p) {
     [[maybe_unused]] const unsigned char *ksb = nullptr, *vsb = nullptr;
     // one head group per row: a stage's 16 rows are contiguous
     [[maybe_unused]] const bool whole_row = HPC == p.nkv;
+    // As a programmatic dependent of the prep kernel, the cache rows it
+    // appends (each segment's last rows) are loaded only after it completed;
+    // the rows before them stream in the meantime.
+    bool dep_done = p.pdl == 0;
 #pragma unroll 1
     while (cur.valid) {
       const int slot = (int)(fill % STAGES);
+      if (!dep_done && cursor_key0(cur) + kKeys >= cur.hi) {
+        asm volatile("griddepcontrol.wait;" ::: "memory");
+        dep_done = true;
+      }
       if (fill >= STAGES) {
         const uint32_t par = (uint32_t)(((fill / STAGES) - 1) & 1);
         if (!mbar_wait_bounded(&empty[slot], par)) {
@@ -560,6 +569,8 @@ decode_kernel(const DecodeParams p) {
     q_v[3] = row_off<Geo>(stage_row<Q8>(2 * t + 9));
   }
 
+  // the queries may come from the prep kernel this grid depends on
+  if (p.pdl) asm volatile("griddepcontrol.wait;" ::: "memory");
 #pragma unroll 1
   while (cur.valid) {
     const int kvh = cur.grp * HPC + h;
@@ -1005,8 +1016,23 @@ int launch_decode_v(DecodeParams& p, long units_hint, int chunk, cudaStream_t st
   p.nctas = (int)ctas;
   p.hpc = HPC;
   p.ngroups = p.nkv / HPC;
-  kern<<<(int)ctas, Geo::THREADS, smem, st>>>(p);
-  ASPIDA_CHECK_LAUNCH();
+  if (p.pdl) {
+    cudaLaunchConfig_t kc = {};
+    kc.gridDim = dim3((unsigned)ctas);
+    kc.blockDim = dim3(Geo::THREADS);
+    kc.dynamicSmemBytes = smem;
+    kc.stream = st;
+    cudaLaunchAttribute ka[1];
+    ka[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    ka[0].val.programmaticStreamSerializationAllowed = 1;
+    kc.attrs = ka;
+    kc.numAttrs = 1;
+    if (cudaError_t e = cudaLaunchKernelEx(&kc, kern, p); e != cudaSuccess)
+      return record_status((int)e);
+  } else {
+    kern<<<(int)ctas, Geo::THREADS, smem, st>>>(p);
+    ASPIDA_CHECK_LAUNCH();
+  }
   // the combine is a programmatic dependent: launched now, it runs its
   // merges as soon as the decode grid completes
   cudaLaunchConfig_t cfg = {};
@@ -1107,8 +1133,9 @@ size_t decode_workspace_size(int B, int nq, int nkv, int hd, int max_kv_len, int
 int decode(const float* q, const float* gate, const void* const* K, const void* const* V,
            const int* pos, const int* max_len, float* out, int B, int nq, int nkv, int hd,
            float scale, int window, float softcap, int max_kv_len, int chunk, void* ws,
-           size_t ws_bytes, cudaStream_t st) {
+           size_t ws_bytes, cudaStream_t st, bool after_prep = false) {
   DecodeParams p{};
+  p.pdl = after_prep ? 1 : 0;
   p.q = q; p.gate = gate;
   p.K = reinterpret_cast<const __half* const*>(K);
   p.V = reinterpret_cast<const __half* const*>(V);

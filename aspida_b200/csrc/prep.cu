@@ -44,6 +44,9 @@ struct PrepArgs {
 // evaluated once per pair (rope_pair), and every store is coalesced.
 __global__ void __launch_bounds__(kPrepWarps * 32) prep_kernel(const PrepArgs a) {
   extern __shared__ float sh_all[];               // [kPrepWarps][hd]
+  // a decode launched as this kernel's programmatic dependent may start now;
+  // it waits for this grid before reading anything it writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long R = (long)blockIdx.x * kPrepWarps + warp;
   if (R >= a.rows) return;

@@ -30,7 +30,7 @@ int launch_prep_lanes(const float* q, const float* k, const float* v, int B, int
 int decode(const float* q, const float* gate, const void* const* K, const void* const* V,
            const int* pos, const int* max_len, float* out, int B, int nq, int nkv, int hd,
            float scale, int window, float softcap, int max_kv_len, int chunk, void* ws,
-           size_t ws_bytes, cudaStream_t st);
+           size_t ws_bytes, cudaStream_t st, bool after_prep);
 size_t decode_workspace_size(int B, int nq, int nkv, int hd, int max_kv_len, int chunk);
 
 
@@ -163,7 +163,7 @@ extern "C" int aspida_attn_step_host(const int* handles, int B, const float* q, 
   if ((rc = decode(dqr, nullptr, reinterpret_cast<const void* const*>(dK),
                    reinterpret_cast<const void* const*>(dV), dpos, dml,
                    out_direct ? out_direct : dout, B, nq, nkv, hd, scale, window, softcap, max_kv,
-                   0, dws, ws, st)))
+                   0, dws, ws, st, true)))
     return rc;
   if (!out_direct &&
       (rc = cuda_status(cudaMemcpyAsync(out, dout, qbytes, cudaMemcpyDeviceToHost, st))))
